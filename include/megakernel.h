@@ -1,0 +1,137 @@
+/*
+ * megakernel.h -- C ABI of libmegakernel (B200 / sm_100a persistent decode
+ * megakernel for Qwen3-0.6B-shaped decoders).
+ *
+ * The first six functions are the drop-in surface of the reference's
+ * `make lib` library (src/megakernel.cu:535-624, bound from Python in
+ * host/bridge.py:39-67); their C signatures and meaning are unchanged.
+ * Everything after them is an additive extension.
+ *
+ * Pointers named d_* are device pointers; all others are host pointers.
+ * Status-returning extensions return MK_OK (0) or a negative MK_ERR_* code.
+ */
+#ifndef MEGAKERNEL_H_
+#define MEGAKERNEL_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MK_OK = 0,
+  MK_ERR_INVALID_ARG = -1, /* bad handle, pointer, token id or size */
+  MK_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+  MK_ERR_TIMEOUT = -3,     /* a bounded in-kernel wait expired */
+  MK_ERR_CAPACITY = -4,    /* position would exceed the KV capacity */
+  MK_ERR_SHAPE = -5,       /* offsets match no compiled model shape */
+  MK_ERR_LAUNCH = -6,      /* cooperative launch impossible (SMs busy, smem) */
+  MK_ERR_OOM = -7          /* device allocation failed */
+};
+
+/* ---- reference surface (src/megakernel.cu:544-622) ---------------------- */
+
+/* Replaces megakernel_init (src/megakernel.cu:544-585).  d_weights: device copy
+ * of the flat binary (caller keeps it alive); offsets: 2 + 11*layers byte
+ * offsets in host/bridge.py:89-96 order.  The model shape is inferred from
+ * the offsets.  Returns NULL on failure (the reference never does). */
+void* megakernel_init(void* d_weights, long long* offsets, int num_offsets);
+
+/* Replaces megakernel_decode (src/megakernel.cu:588-591): feed one token at the
+ * current position, return the greedy next token, advance the position.
+ * Returns -1 on error (see megakernel_last_error). */
+int megakernel_decode(void* handle, int input_token);
+
+/* Replaces megakernel_reset (src/megakernel.cu:594-601): position 0, KV zeroed. */
+void megakernel_reset(void* handle);
+
+/* Replaces megakernel_get_pos (src/megakernel.cu:604-607). */
+int megakernel_get_pos(void* handle);
+
+/* Replaces megakernel_free (src/megakernel.cu:610-617). */
+void megakernel_free(void* handle);
+
+/* Replaces megakernel_sync (src/megakernel.cu:620-622): device synchronize. */
+void megakernel_sync(void);
+
+/* ---- extensions ----------------------------------------------------------- */
+
+typedef struct mk_options {
+  int device;            /* CUDA device ordinal; -1 = current device */
+  int shape_id;          /* 0 d64, 1 d128, 2 tiny; -1 = infer from offsets */
+  int max_seq;           /* KV capacity in positions; 0 = 8448 */
+  int num_ctas;          /* persistent CTAs; 0 = one per SM */
+  long long timeout_ns;  /* bound on every in-kernel wait; 0 = 1 s */
+  int debug_skip_cta;    /* fault-injection hook for tests; -1 = off */
+} mk_options;
+
+/* Fill *opts with the defaults above. */
+void megakernel_default_options(mk_options* opts);
+
+/* megakernel_init with options and a status code. */
+int megakernel_init_ex(void* d_weights, const long long* offsets, int num_offsets,
+                       const mk_options* opts, void** out_handle);
+
+/* Run n_steps decode steps in ONE kernel launch.  Step s feeds d_tokens[s] for
+ * s < n_forced (teacher forcing / prefill) and the previous step's argmax
+ * afterwards.  d_out[s] receives the argmax of step s.  d_logits, if not NULL,
+ * receives [n_steps, vocab] fp32 logits.  stream: cudaStream_t or NULL.
+ * Blocks until the launch finishes; the position advances by n_steps. */
+int megakernel_decode_n(void* handle, const int* d_tokens, int n_forced, int n_steps,
+                        int* d_out, float* d_logits, void* stream);
+
+/* Host-buffer convenience over decode_n: feeds the n_prompt prompt ids, then
+ * generates n_gen tokens greedily (n_prompt + n_gen - 1 steps, one launch)
+ * into out[n_gen].  Copies inputs in and results out itself. */
+int megakernel_generate(void* handle, const int* prompt, int n_prompt, int n_gen, int* out);
+
+/* Capture the fp32 logits of every megakernel_decode call (off by default);
+ * megakernel_get_logits copies the latest ones to out[vocab]. */
+int megakernel_set_logits_capture(void* handle, int enable);
+int megakernel_get_logits(void* handle, float* out);
+
+/* Position control and KV access (KV layout [layers, 2, kv_heads, max_seq,
+ * head_dim] bf16, as src/kv_cache.cuh:9-32).  set_pos lets a caller inject
+ * a prefilled cache. */
+int megakernel_set_pos(void* handle, int pos);
+void* megakernel_kv_ptr(void* handle);
+long long megakernel_kv_bytes(void* handle);
+int megakernel_max_seq(void* handle);
+int megakernel_shape_id(void* handle);
+int megakernel_num_ctas(void* handle);
+
+/* Last error of this handle (MK_OK if none) and a description of a code. */
+int megakernel_last_error(void* handle);
+const char* megakernel_error_string(int code);
+
+/* Phase tracing: while set, every launch writes %globaltimer stamps (ns) for
+ * its first `steps` steps into d_buf[steps][num_ctas][trace_points] (u64,
+ * caller-owned device memory).  Points per layer l (index 7l + k): k=0 the
+ * CTA's copy engine reaches layer l, 1 layer input ready, 2 q/k/v published,
+ * 3 attention merged, 4 x after attention published, 5 MLP hidden published,
+ * 6 layer output published; then 7L lm-head start, 7L+1 lm partial published,
+ * 7L+2 next token known, 7L+3 ns spent waiting on activation hops (thread 0),
+ * 7L+4 SM clock cycles over the step.  steps = 0 turns tracing off. */
+int megakernel_set_trace(void* handle, void* d_buf, int steps);
+int megakernel_trace_points(void* handle);
+/* Profiling aid: sub-phase stamps of layer 1 into d_buf[steps][num_ctas][64]
+ * (needs megakernel_set_trace active; NULL turns it off). */
+int megakernel_set_trace_detail(void* handle, void* d_buf);
+
+/* ---- host-only helpers (no GPU needed) ----------------------------------- */
+
+/* Shape id matching a flat-binary offsets array, or MK_ERR_SHAPE. */
+int megakernel_infer_shape(const long long* offsets, int num_offsets);
+
+/* fp32 RoPE tables [positions, head_dim/2] exactly as the kernel uses them. */
+int megakernel_rope_table(int head_dim, double theta, int positions, float* cos_out,
+                          float* sin_out);
+
+/* Bytes each CTA streams through its shared-memory ring for one step at
+ * position pos (weights + cached K/V): bytes_per_cta[num_ctas]. */
+int megakernel_plan_bytes(int shape_id, int num_ctas, int pos, long long* bytes_per_cta);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEGAKERNEL_H_ */

@@ -1,0 +1,1059 @@
+// The persistent decode megakernel (B200 / sm_100a).
+//
+// Replaces persistent_megakernel (src/megakernel.cu:86-339) and the device op
+// library it inlines (src/gemv.cuh, rmsnorm.cuh, attention.cuh, kv_cache.cuh,
+// sampling.cuh, barriers.cuh).  One cooperative launch of one CTA per SM runs
+// `n_steps` whole decode steps (embedding -> L layers -> final norm -> LM-head
+// argmax -> next input token) without returning to the host.
+//
+// Structure of a CTA:
+//   * warp 16 (producer): walks this CTA's byte stream for every step --
+//     its rows of each weight matrix and its share of the cached K/V -- and
+//     issues 1-D TMA bulk copies into a ring of shared-memory stages, each
+//     completing on a "full" mbarrier.  Weights do not depend on activations,
+//     so the producer runs ahead of the math by up to the ring size, through
+//     every inter-CTA dependency, keeping HBM busy.
+//   * warps 0-15 (consumers): per phase, wait for the activation vector the
+//     phase needs, then do the math on ring stages and release them on an
+//     "empty" mbarrier.
+//
+// Inter-CTA dependencies: every activation element crosses between CTAs as a
+// 64-bit word {tag, fp32 bits} written with one st.relaxed.gpu.  The tag names
+// the (step, layer, phase), so a reader spins on the words it needs until the
+// tags match: no counters, no grid barriers, no fences on the critical path.
+// The reference instead runs 144 atomic grid barriers per token
+// (src/barriers.cuh:38-73).  Every wait is bounded by a globaltimer deadline;
+// on expiry the CTA records an error code and all roles exit.
+#pragma once
+#include "ptx.cuh"
+#include "shapes.cuh"
+
+namespace mk {
+
+enum : int {
+  MK_OK = 0,
+  MK_ERR_INVALID_ARG = -1,
+  MK_ERR_CUDA = -2,
+  MK_ERR_TIMEOUT = -3,
+  MK_ERR_CAPACITY = -4,
+  MK_ERR_SHAPE = -5,
+  MK_ERR_LAUNCH = -6,
+  MK_ERR_OOM = -7,
+};
+
+struct KParams {
+  const __nv_bfloat16* const* w;  // 2 + 11 L weight pointers (offsets order)
+  __nv_bfloat16* kv;              // [L, 2, NKV, max_seq, D]
+  const float* rope_cos;          // [max_seq, D/2]
+  const float* rope_sin;          // [max_seq, D/2]
+  uint64_t* hop;                  // tagged activation words (see HopLayout)
+  int* err;                       // first error code (0 = ok)
+  const int* forced;              // tokens fed at steps 0..n_forced-1
+  int n_forced;                   // >= 1
+  int n_steps;
+  int* out_tokens;                // [n_steps] argmax of each step
+  float* logits;                  // optional [n_steps, V] fp32 logits
+  int pos0;                       // position of step 0
+  uint32_t seq0;                  // tag sequence number of step 0
+  int max_seq;
+  int ncta;
+  int nst;                        // ring stages in use (<= S::NST)
+  long long timeout_ns;
+  int debug_skip_cta;             // >= 0: that CTA never publishes layer-0 x (fault test)
+  uint64_t* trace;                // optional stamps [trace_steps][ncta][Trace::kPoints]
+  int trace_steps;
+  uint64_t* detail;               // optional [trace_steps][ncta][64] sub-phase stamps of layer 1
+};
+
+// Offsets (in 64-bit words) of the tagged activation buffers.
+template <class S>
+struct HopLayout {
+  static constexpr int kAttWords = S::NKV * kMaxChunksPerHead * S::GRP * (S::D + 2);
+  static constexpr long long X = 0;                       // [2][H]  layer input
+  static constexpr long long QKV = X + 2 * S::H;           // [2][QKV]
+  static constexpr long long ATT = QKV + 2 * S::QKV;       // [2][items][GRP][D+2]
+  static constexpr long long XA = ATT + 2LL * kAttWords;   // [2][H]  after attention
+  static constexpr long long HM = XA + 2 * S::H;           // [2][I]  silu(g)*u
+  static constexpr long long LM = HM + 2 * S::I;           // [2][kMaxCtas][2]
+  static constexpr long long TOTAL = LM + 2 * kMaxCtas * 2;
+};
+
+// Tag of phase `k` (0 qkv, 1 att, 2 xa, 3 hm, 4 x-out) of layer `l` at step seq.
+__device__ __forceinline__ uint32_t tag_of(uint32_t seq, int l, int k) {
+  return (seq << 8) | (uint32_t)(l * 5 + k);
+}
+
+// Trace points per (step, CTA): per layer 7 (producer reaches the layer, x
+// ready, qkv published, attention merged, x' published, h published, x''
+// published), then lm start, lm partial published, next token known, the
+// step's total ns consumer thread 0 spent in activation-hop waits, and the
+// SM clock cycles (clock64) elapsed over the step.
+template <class S>
+struct Trace {
+  static constexpr int kPoints = 7 * S::L + 5;
+};
+
+template <class S>
+__device__ __forceinline__ void trace_point(const KParams& P, int t, int cta, int k) {
+  if (P.trace != nullptr && t < P.trace_steps)
+    P.trace[((size_t)t * P.ncta + cta) * Trace<S>::kPoints + k] = globaltimer_ns();
+}
+
+// Sub-phase stamp k of layer 1 (profiling aid; off unless P.detail is set).
+#define MK_DP(k)                                                                      \
+  do {                                                                                \
+    if (P.detail != nullptr && l == 1 && t < P.trace_steps &&                         \
+        (threadIdx.x == 0 || threadIdx.x == kConsumerThreads))                        \
+      P.detail[((size_t)t * P.ncta + blockIdx.x) * 64 + (k)] = globaltimer_ns();      \
+  } while (0)
+
+template <class S>
+struct Smem {
+  float xres[S::H];                   // residual stream x (fp32)
+  float xin[S::XIN];                  // GEMV input vector (normed x, attn, h)
+  // GEMV input split exactly into three bf16 terms, x = hi + mid + lo (each
+  // term keeps 8 mantissa bits, together the 24 of fp32); padded rows keep
+  // the three arrays in different banks.
+  alignas(16) __nv_bfloat16 xs[3][S::XIN + 8];
+  float partw[kConsumerWarps][32];    // per-warp row partials of one GEMV group
+  float rowsum[2][kRowsMax];          // GEMV results of this CTA's rows
+  float qs[S::GRP][S::D];             // normed + roped queries of one KV head
+  float sc[S::GRP][S::SUBP];          // scores / probabilities of one block
+  float pv[kConsumerThreads];         // PV partials (parts x GRP x D)
+  float mrun[S::GRP], lrun[S::GRP], corr[S::GRP];
+  float gq[S::D], gk[S::D];           // q_norm / k_norm gains of the layer
+  float rc[S::D / 2], rs[S::D / 2];   // RoPE cos / sin row of position p
+  __nv_bfloat16 kx[2][S::D];          // K rows not in the ring (prev + current)
+  __nv_bfloat16 vx[2][S::D];
+  float red[kConsumerWarps * 2];
+  int redi[kConsumerWarps];
+  int next_token;
+  volatile int abort_flag;
+  volatile int tokens_done;
+  unsigned long long wait_hop_ns;     // trace accounting (thread 0)
+  const __nv_bfloat16* wtab[S::NOFF]; // weight pointer table (offsets order)
+  alignas(8) uint64_t full[S::NST];
+  alignas(8) uint64_t empty[S::NST];
+};
+
+// ---- failure handling -------------------------------------------------------
+template <class S>
+__device__ __forceinline__ void fail(const KParams& P, Smem<S>& sm, int code) {
+  atomicCAS(P.err, 0, code);
+  sm.abort_flag = 1;
+}
+
+// Bounded spin helper: returns false when the wait must be abandoned
+// (deadline passed, this CTA aborted, or another CTA reported an error).
+struct Spin {
+  uint64_t t0 = 0;
+  uint32_t it = 0;
+  template <class S>
+  __device__ __forceinline__ bool keep_going(const KParams& P, Smem<S>& sm) {
+    if (sm.abort_flag) return false;
+    if ((++it & 63u) == 0) {
+      uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if ((long long)(now - t0) > P.timeout_ns) { fail(P, sm, MK_ERR_TIMEOUT); return false; }
+      // Another CTA's failure: checked rarely, every spinner reads this word.
+      if ((it & 4095u) == 0 && ld_volatile_i32(P.err) != 0) { sm.abort_flag = 1; return false; }
+    }
+    return true;
+  }
+};
+
+template <class S>
+__device__ __forceinline__ bool wait_bar(const KParams& P, Smem<S>& sm, uint64_t* bar, uint32_t parity) {
+  if (mbar_test(bar, parity)) return true;
+  Spin sp;
+  while (!mbar_try_wait(bar, parity)) {
+    if (!sp.keep_going(P, sm)) return false;
+  }
+  return true;
+}
+
+// ---- per-step plan shared by producer and consumers -------------------------
+// This CTA owns rows [s, e) of the concatenated [Wq; Wk; Wv] matrix; the part
+// that falls in tensor m (0 q, 1 k, 2 v) is rows [a, b) of that tensor and
+// starts at output row o.  (Written without arrays so nothing lands in local
+// memory.)
+template <class S>
+__device__ __forceinline__ bool qkv_part(int s, int e, int m, int& a, int& b, int& o) {
+  const int base = m == 0 ? 0 : (m == 1 ? S::Q : S::Q + S::KV);
+  const int len = m == 0 ? S::Q : S::KV;
+  o = max(s, base);
+  const int hi = min(e, base + len);
+  a = o - base;
+  b = hi - base;
+  return o < hi;
+}
+
+// Weight pointer for layer l, key k (0 attn_norm .. 10 w_down), offsets order
+// of src/megakernel.cu:518-532.  Read from the shared-memory copy of the
+// table: almost no L1 is left beside the ring, so a global read would cost an
+// L2 round trip on the critical path.
+#define wptr(l, k) (sm.wtab[2 + 11 * (l) + (k)])
+enum { W_ATTN_NORM = 0, W_Q, W_K, W_V, W_QNORM, W_KNORM, W_O, W_FFN_NORM, W_GATE, W_UP, W_DOWN };
+
+template <class S>
+__device__ __forceinline__ size_t kv_index(int l, int kind, int h, int pos, int max_seq) {
+  return ((((size_t)l * 2 + kind) * S::NKV + h) * (size_t)max_seq + pos) * S::D;
+}
+
+}  // namespace mk
+
+namespace mk {
+
+// ---- producer ---------------------------------------------------------------
+template <class S>
+__device__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ring, int cta) {
+  if ((threadIdx.x & 31) != 0) return;
+  const int N = P.ncta;
+  const uint32_t nst = (uint32_t)P.nst;
+  const uint64_t pol = policy_evict_first();
+  uint32_t k = 0;
+  bool ok = true;
+
+  auto acquire = [&](uint32_t& slot) -> bool {
+    slot = k % nst;
+    const uint32_t ph = (k / nst) & 1u;
+    if (!wait_bar(P, sm, &sm.empty[slot], ph ^ 1u)) { ok = false; return false; }
+    return true;
+  };
+  // Contiguous bytes (LM-head rows, cached K/V): one copy per stage.
+  auto issue = [&](const void* src, uint32_t bytes) {
+    uint32_t slot;
+    if (!ok || !acquire(slot)) return;
+    mbar_arrive_expect_tx(&sm.full[slot], bytes);
+    bulk_g2s(ring + (size_t)slot * S::STB, src, bytes, &sm.full[slot], pol);
+    ++k;
+  };
+  auto issue_rows = [&](const __nv_bfloat16* base, int r0, int r1, int K) {
+    const int rpc = S::STB / (2 * K);
+    for (int r = r0; r < r1 && ok; r += rpc) {
+      const int n = min(rpc, r1 - r);
+      issue(base + (size_t)r * K, (uint32_t)(n * 2 * K));
+    }
+  };
+  // Rows for the tensor-core GEMV: one copy per row, at pitch 2K + 16.
+  auto issue_rows_padded = [&](const __nv_bfloat16* base, int r0, int r1, int K) {
+    const int pitch = 2 * K + kRowPad;
+    const int rpc = S::STB / pitch;
+    for (int r = r0; r < r1 && ok; r += rpc) {
+      const int n = min(rpc, r1 - r);
+      uint32_t slot;
+      if (!acquire(slot)) return;
+      mbar_arrive_expect_tx(&sm.full[slot], (uint32_t)(n * 2 * K));
+      for (int i = 0; i < n; ++i)
+        bulk_g2s(ring + (size_t)slot * S::STB + (size_t)i * pitch, base + (size_t)(r + i) * K,
+                 (uint32_t)(2 * K), &sm.full[slot], pol);
+      ++k;
+    }
+  };
+
+  for (int t = 0; t < P.n_steps && ok; ++t) {
+    const int p = P.pos0 + t;
+    const int nc = chunks_per_head<S>(p);
+    const int nitems = S::NKV * nc;
+    for (int l = 0; l < S::L && ok; ++l) {
+      trace_point<S>(P, t, cta, 7 * l);
+      {
+        int s0, s1;
+        split_rows(S::QKV, N, cta, phase_rot(l, 0, N), s0, s1);
+#pragma unroll
+        for (int m = 0; m < 3; ++m) {
+          int a, b, o;
+          if (qkv_part<S>(s0, s1, m, a, b, o)) issue_rows_padded(wptr(l, W_Q + m), a, b, S::H);
+        }
+      }
+      // Cached K/V of this CTA's attention items.  Positions < p-1 were
+      // written by steps <= t-2 of this launch (or earlier launches); wait
+      // until the consumers have finished step t-2 before reading them.
+      // Position p-1 is read by the consumers directly (written by step t-1).
+      int ilo, ihi;
+      items_of_cta(cta, l, nitems, N, ilo, ihi);
+      for (int i = ilo; i < ihi && ok; ++i) {
+        const int h = i / nc, j = i % nc;
+        int c0, c1;
+        chunk_range(p, nc, j, c0, c1);
+        const int te = min(c1, p - 1);
+        if (c0 >= te) continue;
+        if (t >= 2) {
+          Spin sp;
+          while (sm.tokens_done < t - 1) {
+            if (!sp.keep_going(P, sm)) { ok = false; break; }
+          }
+          if (!ok) break;
+          fence_proxy_async_global();
+        }
+        for (int a = c0; a < te && ok; a += S::SUBP) {
+          const int n = min(S::SUBP, te - a);
+          issue(P.kv + kv_index<S>(l, 0, h, a, P.max_seq), (uint32_t)(n * S::D * 2));
+          issue(P.kv + kv_index<S>(l, 1, h, a, P.max_seq), (uint32_t)(n * S::D * 2));
+        }
+      }
+      int r0, r1;
+      MK_DP(24);
+      split_rows(S::H, N, cta, phase_rot(l, 1, N), r0, r1);
+      issue_rows_padded(wptr(l, W_O), r0, r1, S::Q);
+      MK_DP(25);
+      split_rows(S::I, N, cta, phase_rot(l, 2, N), r0, r1);
+      issue_rows_padded(wptr(l, W_GATE), r0, r1, S::H);
+      MK_DP(26);
+      issue_rows_padded(wptr(l, W_UP), r0, r1, S::H);
+      MK_DP(27);
+      split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
+      issue_rows_padded(wptr(l, W_DOWN), r0, r1, S::I);
+      MK_DP(28);
+    }
+    int r0, r1;
+    split_rows(S::V, N, cta, phase_rot(S::L, 4, N), r0, r1);
+    issue_rows(sm.wtab[0], r0, r1, S::H);
+  }
+  if (!ok) {
+    // Abandoned: wait (bounded) for the copies already in flight so that no
+    // bulk copy lands in shared memory after this CTA has exited.
+    const uint32_t first = k > nst ? k - nst : 0;
+    for (uint32_t c = first; c < k; ++c) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&sm.full[c % nst], (c / nst) & 1u)) {
+        if ((long long)(globaltimer_ns() - t0) > P.timeout_ns) break;
+      }
+    }
+  }
+}
+
+}  // namespace mk
+
+namespace mk {
+
+// ---- consumer helpers (all 512 consumer threads call these) -----------------
+
+// Spin on n tagged words src[i] until each carries `tag`; store the fp32
+// payloads to dst[i].  Each thread first issues all of its loads (up to
+// kBatch in flight) and only then checks tags, so a hop costs about one L2
+// round trip instead of one per word.  No barrier inside.
+template <class S>
+__device__ __forceinline__ void wait_tagged(const KParams& P, Smem<S>& sm, const uint64_t* src,
+                                            int n, uint32_t tag, float* dst) {
+  constexpr int kBatch = 8;
+  const uint64_t tw0 = (P.trace != nullptr && threadIdx.x == 0) ? globaltimer_ns() : 0;
+  for (int base = threadIdx.x; base < n; base += kConsumerThreads * kBatch) {
+    uint64_t v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = base + k * kConsumerThreads;
+      v[k] = i < n ? ld_relaxed(src + i) : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = base + k * kConsumerThreads;
+      if (i >= n) break;
+      if ((uint32_t)(v[k] >> 32) != tag) {
+        Spin sp;
+        do {
+          if (!sp.keep_going(P, sm)) break;
+          v[k] = ld_relaxed(src + i);
+        } while ((uint32_t)(v[k] >> 32) != tag);
+      }
+      dst[i] = __uint_as_float((uint32_t)v[k]);
+    }
+  }
+  if (tw0 != 0) sm.wait_hop_ns += globaltimer_ns() - tw0;
+}
+
+// One tagged word, returned as float.
+template <class S>
+__device__ __forceinline__ float wait_word(const KParams& P, Smem<S>& sm, const uint64_t* src,
+                                           uint32_t tag) {
+  uint64_t v = ld_relaxed(src);
+  if ((uint32_t)(v >> 32) != tag) {
+    Spin sp;
+    do {
+      if (!sp.keep_going(P, sm)) break;
+      v = ld_relaxed(src);
+    } while ((uint32_t)(v >> 32) != tag);
+  }
+  return __uint_as_float((uint32_t)v);
+}
+
+// Block-wide fp32 sum over the consumer threads (fixed reduction order).
+template <class S>
+__device__ __forceinline__ float consumer_sum(Smem<S>& sm, float v) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) sm.red[warp] = v;
+  consumer_sync(kConsumerThreads);
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) s += sm.red[w];
+  consumer_sync(kConsumerThreads);
+  return s;
+}
+
+// xs[0..2][i] = bf16 terms hi, mid, lo of x with hi + mid + lo == x to fp32
+// precision.  The tensor-core GEMV multiplies all three terms.
+template <class S>
+__device__ __forceinline__ void split_one(Smem<S>& sm, int i, float x) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+  const float r1 = x - __bfloat162float(hi);
+  const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(mid);
+  sm.xs[0][i] = hi;
+  sm.xs[1][i] = mid;
+  sm.xs[2][i] = __float2bfloat16_rn(r2);
+}
+template <class S>
+__device__ __forceinline__ void split_xin(Smem<S>& sm, int n) {
+  for (int i = threadIdx.x; i < n; i += kConsumerThreads) split_one(sm, i, sm.xin[i]);
+  consumer_sync(kConsumerThreads);
+}
+
+// Norm gains are loaded into registers BEFORE the caller waits for the
+// activation hop, so their global-memory latency overlaps the wait.
+template <class S>
+struct GainRegs {
+  static constexpr int kPer = (S::H + kConsumerThreads - 1) / kConsumerThreads;
+  float g[kPer];
+  __device__ __forceinline__ void load(const __nv_bfloat16* gp) {
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) {
+      const int i = threadIdx.x + e * kConsumerThreads;
+      g[e] = i < S::H ? __bfloat162float(gp[i]) : 0.f;
+    }
+  }
+};
+
+// xin = g * (xres * rsqrt(mean(xres^2) + eps))   (Qwen3RMSNorm order), also
+// split into xs.  Replaces rmsnorm_float_in (src/rmsnorm.cuh:87-108); computed
+// redundantly in every CTA and kept in shared memory, never written back.
+template <class S>
+__device__ __forceinline__ void rmsnorm_to_xin(Smem<S>& sm, const GainRegs<S>& gr) {
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < S::H; i += kConsumerThreads) ss += sm.xres[i] * sm.xres[i];
+  ss = consumer_sum(sm, ss);
+  const float r = rsqrtf(ss / (float)S::H + 1e-6f);
+#pragma unroll
+  for (int e = 0; e < GainRegs<S>::kPer; ++e) {
+    const int i = threadIdx.x + e * kConsumerThreads;
+    if (i < S::H) {
+      const float v = gr.g[e] * (sm.xres[i] * r);
+      sm.xin[i] = v;
+      split_one(sm, i, v);
+    }
+  }
+  consumer_sync(kConsumerThreads);
+}
+
+// out[r - r0] = W[r, :] . x for rows [r0, r1) of a row-major bf16 matrix
+// with K columns, whose rows the producer placed in consecutive ring stages
+// at pitch 2K + 16.  Replaces gemv_block / gemv_qkv / gemv_gate_up_silu
+// (src/gemv.cuh:36-279) with warp-level tensor-core MMAs:
+//   A = 16 weight rows x 16 columns (ldmatrix from the stage),
+//   B = 16 columns x 8, whose columns 0..2 are the hi/mid/lo bf16 terms of x,
+//   so row r's dot product is D[r][0] + D[r][1] + D[r][2] in fp32.
+// Warp w takes the 16-column slices ks = w, w + 16, ...; the 16 warps'
+// partial sums are added in a fixed order.  Up to 4 stages (<= 32 rows) are
+// consumed per group.  All consumer threads must call this.
+template <class S, int K>
+__device__ __forceinline__ void gemv_mma(const KParams& P, Smem<S>& sm, const uint8_t* ring,
+                                         uint32_t& kc, int r0, int r1, float* out) {
+  constexpr int PITCH = S::template pitch<K>();
+  constexpr int RPC = S::template rows_per_stage<K>();
+  static_assert(RPC >= 1, "stage too small");
+  constexpr int GCH0 = 32 / RPC;
+  constexpr int GCH = GCH0 < 1 ? 1 : (GCH0 > 4 ? 4 : GCH0);
+  constexpr int GROWS = GCH * RPC;                 // rows per group (<= 32)
+  static_assert(GROWS <= 32, "two 16-row tiles per group");
+  constexpr int KS = K / 16;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const uint32_t nst = (uint32_t)P.nst;
+  const uint32_t* xs0 = reinterpret_cast<const uint32_t*>(&sm.xs[g < 3 ? g : 0][0]);
+  for (int g0 = r0; g0 < r1; g0 += GROWS) {
+    const int n = min(GROWS, r1 - g0);
+    const int nch = (n + RPC - 1) / RPC;
+    const uint32_t slot0 = kc % nst, ph0 = (kc / nst) & 1u;
+    bool ok = true;
+    for (int c = 0; c < nch; ++c) {
+      uint32_t sl = slot0 + c, ph = ph0;
+      if (sl >= nst) { sl -= nst; ph ^= 1u; }
+      ok = wait_bar(P, sm, &sm.full[sl], ph) && ok;
+    }
+    ok = __all_sync(0xffffffffu, ok);
+#pragma unroll
+    for (int tile = 0; tile < 2; ++tile) {
+      if (tile * 16 >= n) break;
+      // ldmatrix row pointer of this lane: matrices (rows 0-7 | 8-15) x (k 0-7 | 8-15).
+      int lrow = tile * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+      if (lrow >= n) lrow = 0;  // rows past the segment: any valid address, result unused
+      const int c = lrow / RPC, rin = lrow - c * RPC;
+      uint32_t sl = slot0 + c;
+      if (sl >= nst) sl -= nst;
+      const uint32_t abase =
+          smem_u32(ring + (size_t)sl * S::STB + (size_t)rin * PITCH) + (uint32_t)((lane >> 4) * 16);
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+      if (ok) {
+        for (int ks = warp; ks < KS; ks += kConsumerWarps) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(abase + ks * 32, a0, a1, a2, a3);
+          const uint32_t b0 = g < 3 ? xs0[(ks * 16 + 2 * tq) >> 1] : 0u;
+          const uint32_t b1 = g < 3 ? xs0[(ks * 16 + 2 * tq + 8) >> 1] : 0u;
+          mma_bf16_16816(d0, d1, d2, d3, a0, a1, a2, a3, b0, b1);
+        }
+      }
+      // Lane (g, tq=0) holds columns 0,1 of rows g, g+8; lane (g, tq=1) column 2.
+      float s0 = d0 + d1, s1 = d2 + d3;
+      s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+      if (tq == 0) {
+        sm.partw[warp][tile * 16 + g] = s0;
+        sm.partw[warp][tile * 16 + g + 8] = s1;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      for (int c = 0; c < nch; ++c) {
+        uint32_t sl = slot0 + c;
+        if (sl >= nst) sl -= nst;
+        mbar_arrive(&sm.empty[sl]);
+      }
+    }
+    kc += nch;
+    consumer_sync(kConsumerThreads);
+    if (threadIdx.x < n) {
+      float tsum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) tsum += sm.partw[w][threadIdx.x];
+      out[g0 - r0 + threadIdx.x] = tsum;
+    }
+    consumer_sync(kConsumerThreads);
+  }
+}
+
+// LM head over rows [r0, r1) of the tied embedding: per-warp running argmax
+// (strictly greater => lowest index kept), optional fp32 logits.  Replaces
+// lm_head_argmax_phase1 (src/sampling.cuh:32-89): a warp reads whole 2*H-byte
+// rows from shared memory instead of one thread walking each row.
+template <class S>
+__device__ __forceinline__ void lm_rows(const KParams& P, Smem<S>& sm, const uint8_t* ring,
+                                        uint32_t& kc, int r0, int r1, float* logits_row0,
+                                        float& best_v, int& best_i) {
+  constexpr int PPR = S::H / 256;
+  constexpr int RB = 2 * S::H;
+  constexpr int RPC = S::STB / RB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t nst = (uint32_t)P.nst;
+  float xr[PPR][8];
+#pragma unroll
+  for (int q = 0; q < PPR; ++q) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) xr[q][e] = sm.xin[q * 256 + lane * 8 + e];
+  }
+  for (int cr = r0; cr < r1; cr += RPC) {
+    const int n = min(RPC, r1 - cr);
+    const uint32_t slot = kc % nst, ph = (kc / nst) & 1u;
+    if (__all_sync(0xffffffffu, wait_bar(P, sm, &sm.full[slot], ph))) {
+      const uint8_t* st = ring + (size_t)slot * S::STB + lane * 16;
+      const int rel = cr - r0;
+      for (int r = ((warp - rel) % kConsumerWarps + kConsumerWarps) % kConsumerWarps; r < n;
+           r += kConsumerWarps) {
+        float a = 0.f;
+#pragma unroll
+        for (int q = 0; q < PPR; ++q)
+          a += dot8(*reinterpret_cast<const uint4*>(st + (size_t)r * RB + q * 512), xr[q]);
+        a = warp_sum(a);
+        const int row = cr + r;
+        if (a > best_v) { best_v = a; best_i = row; }
+        if (logits_row0 != nullptr && lane == 0) logits_row0[row] = a;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[slot]);
+    ++kc;
+  }
+}
+
+}  // namespace mk
+
+namespace mk {
+
+// Online-softmax update over n positions whose K and V rows (D bf16 each) sit
+// contiguously in shared memory.  Scores: warp per position, lanes over D.
+// PV: thread (part, g, d) sums positions = part (mod parts).  The running
+// (m, l) live in sm.mrun/lrun; the PV accumulator stays in `acc`.
+template <class S>
+__device__ __forceinline__ void attend_block(Smem<S>& sm, const __nv_bfloat16* K,
+                                             const __nv_bfloat16* V, int n, float& acc) {
+  constexpr int D = S::D, GRP = S::GRP;
+  constexpr int EPL = D / 32;  // elements per lane
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float scale = (D == 64) ? 0.125f : 0.08838834764831845f;  // D^-0.5
+  for (int pos = warp; pos < n; pos += kConsumerWarps) {
+    float kf[EPL];
+    if constexpr (EPL == 2) {
+      uint32_t w = *reinterpret_cast<const uint32_t*>(K + (size_t)pos * D + lane * 2);
+      kf[0] = bf_lo(w); kf[1] = bf_hi(w);
+    } else {
+      uint2 w = *reinterpret_cast<const uint2*>(K + (size_t)pos * D + lane * 4);
+      kf[0] = bf_lo(w.x); kf[1] = bf_hi(w.x); kf[2] = bf_lo(w.y); kf[3] = bf_hi(w.y);
+    }
+#pragma unroll
+    for (int g = 0; g < GRP; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) s = fmaf(sm.qs[g][lane * EPL + e], kf[e], s);
+      s = warp_sum(s);
+      if (lane == 0) sm.sc[g][pos] = s * scale;
+    }
+  }
+  consumer_sync(kConsumerThreads);
+  if (warp < GRP) {
+    const int g = warp;
+    float mx = -INFINITY;
+    for (int pos = lane; pos < n; pos += 32) mx = fmaxf(mx, sm.sc[g][pos]);
+    mx = warp_max(mx);
+    const float mold = sm.mrun[g];
+    const float mnew = fmaxf(mold, mx);
+    const float c = expf(mold - mnew);
+    float sum = 0.f;
+    for (int pos = lane; pos < n; pos += 32) {
+      float e = expf(sm.sc[g][pos] - mnew);
+      sm.sc[g][pos] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    __syncwarp();
+    if (lane == 0) {
+      sm.lrun[g] = sm.lrun[g] * c + sum;
+      sm.mrun[g] = mnew;
+      sm.corr[g] = c;
+    }
+  }
+  consumer_sync(kConsumerThreads);
+  {
+    constexpr int GD = GRP * D;
+    constexpr int PARTS = kConsumerThreads / GD;
+    const int tid = threadIdx.x;
+    const int part = tid / GD, g = (tid / D) % GRP, d = tid % D;
+    float a = 0.f;
+    for (int pos = part; pos < n; pos += PARTS)
+      a = fmaf(sm.sc[g][pos], __bfloat162float(V[(size_t)pos * D + d]), a);
+    acc = acc * sm.corr[g] + a;
+  }
+  consumer_sync(kConsumerThreads);
+}
+
+// Attention item (KV head h, chunk j of nc) for layer l at position p: QK-norm,
+// RoPE, append of the current K/V (last chunk only), online softmax over the
+// chunk, and a tagged partial {acc[GRP][D], m, l}.  Replaces qk_rmsnorm_inplace
+// (src/rmsnorm.cuh:57-84), apply_rope_inplace (src/attention.cuh:22-44),
+// append_kv (src/kv_cache.cuh:58-78) and warp_attention (src/attention.cuh:100-167).
+template <class S>
+__device__ void attention_item(const KParams& P, Smem<S>& sm, const uint8_t* ring, uint32_t& kc,
+                               int t, int l, int p, uint32_t seq, int h, int j, int nc, int item) {
+  constexpr int D = S::D, GRP = S::GRP, HALF = D / 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint64_t* qkv = P.hop + HopLayout<S>::QKV + (size_t)(l & 1) * S::QKV;
+  const uint32_t tq = tag_of(seq, l, 0);
+  const uint32_t nst = (uint32_t)P.nst;
+  int c0, c1;
+  chunk_range(p, nc, j, c0, c1);
+  const bool last = (j == nc - 1);
+  const bool prev = (p >= 1) && (c0 <= p - 1) && (p - 1 < c1);
+  const int te = min(c1, p - 1);
+
+  // Side inputs that do not depend on this step's activations are loaded into
+  // registers first, so their latency overlaps the wait for q, k, v:
+  // threads [0, D) gains, [D, D + D/2) RoPE row, [256, 256 + D) K/V of p-1.
+  float pre0 = 0.f, pre1 = 0.f;
+  unsigned short prek = 0, prev_v = 0;
+  if (tid < D) {
+    pre0 = __bfloat162float(wptr(l, W_QNORM)[tid]);
+    pre1 = __bfloat162float(wptr(l, W_KNORM)[tid]);
+  } else if (tid < D + HALF) {
+    pre0 = P.rope_cos[(size_t)p * HALF + (tid - D)];
+    pre1 = P.rope_sin[(size_t)p * HALF + (tid - D)];
+  } else if (prev && tid >= 256 && tid < 256 + D) {
+    // Written by the previous step (possibly another CTA): read through L2.
+    const unsigned short* kvu = reinterpret_cast<const unsigned short*>(P.kv);
+    prek = __ldcg(kvu + kv_index<S>(l, 0, h, p - 1, P.max_seq) + (tid - 256));
+    prev_v = __ldcg(kvu + kv_index<S>(l, 1, h, p - 1, P.max_seq) + (tid - 256));
+  }
+  // Raw q (GRP heads), k, v of this KV head -> sm.pv as scratch [GRP+2][D].
+  float* raw = sm.pv;
+  wait_tagged(P, sm, qkv + h * GRP * D, GRP * D, tq, raw);
+  wait_tagged(P, sm, qkv + S::Q + h * D, D, tq, raw + GRP * D);
+  wait_tagged(P, sm, qkv + S::Q + S::KV + h * D, D, tq, raw + (GRP + 1) * D);
+  if (tid < D) {
+    sm.gq[tid] = pre0;
+    sm.gk[tid] = pre1;
+  } else if (tid < D + HALF) {
+    sm.rc[tid - D] = pre0;
+    sm.rs[tid - D] = pre1;
+  } else if (prev && tid >= 256 && tid < 256 + D) {
+    sm.kx[0][tid - 256] = __ushort_as_bfloat16(prek);
+    sm.vx[0][tid - 256] = __ushort_as_bfloat16(prev_v);
+  }
+  if (tid < GRP) { sm.mrun[tid] = -INFINITY; sm.lrun[tid] = 0.f; }
+  consumer_sync(kConsumerThreads);
+  MK_DP(4);
+
+  // Per-head RMSNorm (q_norm / k_norm gains) then rotate-half RoPE at p.
+  if (warp <= GRP) {
+    float* x = raw + warp * D;
+    const float* gn = warp < GRP ? sm.gq : sm.gk;
+    float ss = 0.f;
+    for (int d = lane; d < D; d += 32) ss += x[d] * x[d];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)D + 1e-6f);
+    float y[D / 32];
+#pragma unroll
+    for (int e = 0; e < D / 32; ++e) y[e] = gn[lane + 32 * e] * (x[lane + 32 * e] * r);
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < D / 32; ++e) x[lane + 32 * e] = y[e];
+    __syncwarp();
+    for (int d = lane; d < HALF; d += 32) {
+      const float x0 = x[d], x1 = x[d + HALF], c = sm.rc[d], s = sm.rs[d];
+      const float o0 = x0 * c - x1 * s;
+      const float o1 = x1 * c + x0 * s;
+      if (warp < GRP) {
+        sm.qs[warp][d] = o0;
+        sm.qs[warp][d + HALF] = o1;
+      } else {
+        sm.kx[1][d] = __float2bfloat16_rn(o0);
+        sm.kx[1][d + HALF] = __float2bfloat16_rn(o1);
+      }
+    }
+  } else if (warp == GRP + 1) {
+    const float* v = raw + (GRP + 1) * D;
+    for (int d = lane; d < D; d += 32) sm.vx[1][d] = __float2bfloat16_rn(v[d]);
+  }
+  consumer_sync(kConsumerThreads);
+  if (last && tid < D) {
+    // Append the current K/V (bf16) at position p; later steps read it.
+    P.kv[kv_index<S>(l, 0, h, p, P.max_seq) + tid] = sm.kx[1][tid];
+    P.kv[kv_index<S>(l, 1, h, p, P.max_seq) + tid] = sm.vx[1][tid];
+    fence_proxy_async_global();
+    __threadfence();
+  }
+  MK_DP(5);
+
+  float acc = 0.f;
+  // Positions held outside the ring: p-1 (slot 0) and the current p (slot 1).
+  {
+    const int s0 = prev ? 0 : 1;
+    const int ne = (prev ? 1 : 0) + (last ? 1 : 0);
+    if (ne > 0) attend_block(sm, &sm.kx[s0][0], &sm.vx[s0][0], ne, acc);
+  }
+  MK_DP(6);
+  // Cached positions [c0, te) streamed through the ring as (K, V) stage pairs.
+  for (int a = c0; a < te; a += S::SUBP) {
+    const int n = min(S::SUBP, te - a);
+    const uint32_t sk = kc % nst, pk = (kc / nst) & 1u;
+    const uint32_t sv = (kc + 1) % nst, pv = ((kc + 1) / nst) & 1u;
+    const bool okk = wait_bar(P, sm, &sm.full[sk], pk);
+    const bool okv = okk && wait_bar(P, sm, &sm.full[sv], pv);
+    if (!consumer_any(kConsumerThreads, !(okk && okv))) {
+      attend_block(sm, reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sk * S::STB),
+                   reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sv * S::STB), n, acc);
+    }
+    if (lane == 0) { mbar_arrive(&sm.empty[sk]); mbar_arrive(&sm.empty[sv]); }
+    kc += 2;
+  }
+  MK_DP(7);
+  sm.pv[tid] = acc;
+  consumer_sync(kConsumerThreads);
+  uint64_t* out = P.hop + HopLayout<S>::ATT + (size_t)(l & 1) * HopLayout<S>::kAttWords +
+                  (size_t)item * GRP * (D + 2);
+  const uint32_t ta = tag_of(seq, l, 1);
+  if (tid < GRP * D) {
+    constexpr int GD = GRP * D, PARTS = kConsumerThreads / GD;
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < PARTS; ++q) s += sm.pv[q * GD + tid];
+    const int g = tid / D, d = tid % D;
+    st_tagged(out + g * (D + 2) + d, ta, __float_as_uint(s));
+  }
+  if (tid < GRP) {
+    st_tagged(out + tid * (D + 2) + D, ta, __float_as_uint(sm.mrun[tid]));
+    st_tagged(out + tid * (D + 2) + D + 1, ta, __float_as_uint(sm.lrun[tid]));
+  }
+  consumer_sync(kConsumerThreads);
+}
+
+// Merge the split-KV partials of layer l into xin[Q] (every CTA, redundantly):
+// out = sum_j exp(m_j - M) acc_j / sum_j exp(m_j - M) l_j, as an online merge.
+// Thread t owns EPT consecutive outputs of one query head; it issues the loads
+// of two chunks' {m, l, acc} at a time, so short contexts (nc <= 2) cost one
+// L2 round trip.  Also writes the bf16 split terms of each output.
+template <class S>
+__device__ __forceinline__ void merge_attention(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc) {
+  constexpr int D = S::D, GRP = S::GRP;
+  constexpr int EPT = S::Q >= kConsumerThreads ? S::Q / kConsumerThreads : 1;
+  static_assert(D % EPT == 0, "a thread's outputs stay inside one head");
+  const uint64_t* att = P.hop + HopLayout<S>::ATT + (size_t)(l & 1) * HopLayout<S>::kAttWords;
+  const uint32_t ta = tag_of(seq, l, 1);
+  const int e0 = threadIdx.x * EPT;
+  if (e0 >= S::Q) return;
+  const int qh = e0 / D, d0 = e0 % D, g = qh % GRP;
+  const size_t stride = (size_t)GRP * (D + 2);
+  const uint64_t* b = att + ((size_t)(qh / GRP) * nc * GRP + g) * (D + 2);
+  float M = -INFINITY, den = 0.f, acc[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) acc[k] = 0.f;
+  for (int j0 = 0; j0 < nc; j0 += 2) {
+    uint64_t w[2][EPT + 2];
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      if (j0 + jj >= nc) break;
+      const uint64_t* bj = b + (size_t)(j0 + jj) * stride;
+      w[jj][0] = ld_relaxed(bj + D);
+      w[jj][1] = ld_relaxed(bj + D + 1);
+#pragma unroll
+      for (int k = 0; k < EPT; ++k) w[jj][2 + k] = ld_relaxed(bj + d0 + k);
+    }
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      if (j0 + jj >= nc) break;
+      const uint64_t* bj = b + (size_t)(j0 + jj) * stride;
+      float f[EPT + 2];
+#pragma unroll
+      for (int k = 0; k < EPT + 2; ++k) {
+        const uint64_t* src = bj + (k == 0 ? D : k == 1 ? D + 1 : d0 + k - 2);
+        f[k] = (uint32_t)(w[jj][k] >> 32) == ta ? __uint_as_float((uint32_t)w[jj][k])
+                                                : wait_word(P, sm, src, ta);
+      }
+      const float mn = fmaxf(M, f[0]);
+      const float c = expf(M - mn), cj = expf(f[0] - mn);
+      den = den * c + f[1] * cj;
+#pragma unroll
+      for (int k = 0; k < EPT; ++k) acc[k] = acc[k] * c + f[2 + k] * cj;
+      M = mn;
+    }
+  }
+  const float inv = 1.f / den;
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    sm.xin[e0 + k] = acc[k] * inv;
+    split_one(sm, e0 + k, acc[k] * inv);
+  }
+}
+
+}  // namespace mk
+
+namespace mk {
+
+template <class S>
+__device__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, int cta) {
+  const int N = P.ncta, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint32_t kc = 0;
+  int tok = P.forced[0];
+  for (int t = 0; t < P.n_steps; ++t) {
+    const int p = P.pos0 + t;
+    const uint32_t seq = P.seq0 + (uint32_t)t;
+    const int nc = chunks_per_head<S>(p);
+    const int nitems = S::NKV * nc;
+    const long long clk0 = clock64();
+    {
+      const __nv_bfloat16* er = sm.wtab[0] + (size_t)tok * S::H;
+      for (int i = tid; i < S::H; i += kConsumerThreads) sm.xres[i] = __bfloat162float(er[i]);
+    }
+    consumer_sync(kConsumerThreads);
+    for (int l = 0; l < S::L; ++l) {
+      // ---- P1: x -> RMSNorm -> q, k, v rows --------------------------------
+      GainRegs<S> gains;
+      gains.load(wptr(l, W_ATTN_NORM));
+      if (l > 0)
+        wait_tagged(P, sm, P.hop + HopLayout<S>::X + (size_t)(l & 1) * S::H, S::H,
+                    tag_of(seq, l - 1, 4), sm.xres);
+      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+      if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 1);
+      rmsnorm_to_xin(sm, gains);
+      MK_DP(1);
+      {
+        int s0, s1;
+        split_rows(S::QKV, N, cta, phase_rot(l, 0, N), s0, s1);
+#pragma unroll
+        for (int m = 0; m < 3; ++m) {
+          int a, b, o;
+          if (qkv_part<S>(s0, s1, m, a, b, o))
+            gemv_mma<S, S::H>(P, sm, ring, kc, a, b, sm.rowsum[0] + (o - s0));
+        }
+        MK_DP(2);
+        uint64_t* dst = P.hop + HopLayout<S>::QKV + (size_t)(l & 1) * S::QKV;
+        const uint32_t tg = tag_of(seq, l, 0);
+        for (int r = tid; r < s1 - s0; r += kConsumerThreads)
+          st_tagged(dst + s0 + r, tg, __float_as_uint(sm.rowsum[0][r]));
+        consumer_sync(kConsumerThreads);
+        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 2);
+      }
+      // ---- P2: attention items owned by this CTA ------------------------------
+      {
+        int ilo, ihi;
+        items_of_cta(cta, l, nitems, N, ilo, ihi);
+        for (int i = ilo; i < ihi; ++i)
+          attention_item<S>(P, sm, ring, kc, t, l, p, seq, i / nc, i % nc, nc, i);
+      }
+      // ---- P3: merge -> O projection + residual --------------------------------
+      MK_DP(8);
+      merge_attention<S>(P, sm, l, seq, nc);
+      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+      if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 3);
+      {
+        int r0, r1;
+        split_rows(S::H, N, cta, phase_rot(l, 1, N), r0, r1);
+        gemv_mma<S, S::Q>(P, sm, ring, kc, r0, r1, sm.rowsum[0]);
+        MK_DP(10);
+        uint64_t* dst = P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H;
+        const uint32_t tg = tag_of(seq, l, 2);
+        for (int r = tid; r < r1 - r0; r += kConsumerThreads)
+          st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
+        consumer_sync(kConsumerThreads);
+        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 4);
+      }
+      // ---- P4: x' -> RMSNorm -> silu(gate) * up ---------------------------------
+      gains.load(wptr(l, W_FFN_NORM));
+      wait_tagged(P, sm, P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H, S::H,
+                  tag_of(seq, l, 2), sm.xres);
+      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+      MK_DP(12);
+      rmsnorm_to_xin(sm, gains);
+      MK_DP(13);
+      {
+        int r0, r1;
+        split_rows(S::I, N, cta, phase_rot(l, 2, N), r0, r1);
+        gemv_mma<S, S::H>(P, sm, ring, kc, r0, r1, sm.rowsum[0]);
+        MK_DP(14);
+        gemv_mma<S, S::H>(P, sm, ring, kc, r0, r1, sm.rowsum[1]);
+        MK_DP(15);
+        uint64_t* dst = P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I;
+        const uint32_t tg = tag_of(seq, l, 3);
+        for (int r = tid; r < r1 - r0; r += kConsumerThreads) {
+          const float g = sm.rowsum[0][r];
+          const float u = sm.rowsum[1][r];
+          const float hval = (g / (1.0f + expf(-g))) * u;
+          st_tagged(dst + r0 + r, tg, __float_as_uint(hval));
+        }
+        consumer_sync(kConsumerThreads);
+        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 5);
+      }
+      // ---- P5: h -> down projection + residual --------------------------------
+      wait_tagged(P, sm, P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I, S::I,
+                  tag_of(seq, l, 3), sm.xin);
+      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+      split_xin(sm, S::I);
+      MK_DP(17);
+      {
+        int r0, r1;
+        split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
+        gemv_mma<S, S::I>(P, sm, ring, kc, r0, r1, sm.rowsum[0]);
+        MK_DP(18);
+        uint64_t* dst = P.hop + HopLayout<S>::X + (size_t)((l + 1) & 1) * S::H;
+        const uint32_t tg = tag_of(seq, l, 4);
+        const bool skip = (l == 0 && cta == P.debug_skip_cta);
+        if (!skip)
+          for (int r = tid; r < r1 - r0; r += kConsumerThreads)
+            st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
+        consumer_sync(kConsumerThreads);
+        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 6);
+      }
+    }
+    // ---- final RMSNorm -> LM head -> argmax ------------------------------------
+    GainRegs<S> fgains;
+    fgains.load(sm.wtab[1]);
+    wait_tagged(P, sm, P.hop + HopLayout<S>::X + (size_t)(S::L & 1) * S::H, S::H,
+                tag_of(seq, S::L - 1, 4), sm.xres);
+    if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+    rmsnorm_to_xin(sm, fgains);
+    if (tid == 0) trace_point<S>(P, t, cta, 7 * S::L);
+    {
+      int r0, r1;
+      split_rows(S::V, N, cta, phase_rot(S::L, 4, N), r0, r1);
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      float* lrow = P.logits ? P.logits + (size_t)t * S::V : nullptr;
+      lm_rows<S>(P, sm, ring, kc, r0, r1, lrow, bv, bi);
+      if (lane == 0) { sm.red[warp] = bv; sm.redi[warp] = bi; }
+      consumer_sync(kConsumerThreads);
+      uint64_t* lm = P.hop + HopLayout<S>::LM + (size_t)(t & 1) * kMaxCtas * 2;
+      const uint32_t tg = tag_of(seq, S::L, 0);
+      if (tid == 0) {
+        float v = sm.red[0];
+        int ix = sm.redi[0];
+        for (int w = 1; w < kConsumerWarps; ++w)
+          if (sm.red[w] > v || (sm.red[w] == v && sm.redi[w] < ix)) { v = sm.red[w]; ix = sm.redi[w]; }
+        st_tagged(lm + 2 * cta, tg, __float_as_uint(v));
+        st_tagged(lm + 2 * cta + 1, tg, (uint32_t)ix);
+        trace_point<S>(P, t, cta, 7 * S::L + 1);
+      }
+      // Every CTA reduces all CTAs' (max, index) pairs: lowest index wins ties.
+      float* pairs = &sm.partw[0][0];
+      for (int c = tid; c < N; c += kConsumerThreads) {
+        pairs[c] = wait_word(P, sm, lm + 2 * c, tg);
+        pairs[kMaxCtas + c] = wait_word(P, sm, lm + 2 * c + 1, tg);
+      }
+      consumer_sync(kConsumerThreads);
+      if (warp == 0) {
+        float v = -INFINITY;
+        int ix = 0x7fffffff;
+        for (int c = lane; c < N; c += 32) {
+          const float cv = pairs[c];
+          const int ci = (int)__float_as_uint(pairs[kMaxCtas + c]);
+          if (cv > v || (cv == v && ci < ix)) { v = cv; ix = ci; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+          if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
+        }
+        if (lane == 0) sm.next_token = ix;
+      }
+      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+      const int best = sm.next_token;
+      if (cta == 0 && tid == 0) P.out_tokens[t] = best;
+      tok = (t + 1 < P.n_forced) ? P.forced[t + 1] : best;
+      if (tok < 0 || tok >= S::V) tok = 0;  // forced ids are range-checked on the host
+      if (tid == 0) {
+        trace_point<S>(P, t, cta, 7 * S::L + 2);
+        if (P.trace != nullptr && t < P.trace_steps) {
+          uint64_t* tr = P.trace + ((size_t)t * P.ncta + cta) * Trace<S>::kPoints;
+          tr[7 * S::L + 3] = sm.wait_hop_ns;
+          tr[7 * S::L + 4] = (uint64_t)(clock64() - clk0);
+        }
+        sm.wait_hop_ns = 0;
+        __threadfence();
+        sm.tokens_done = t + 1;
+      }
+    }
+  }
+}
+
+template <class S>
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ KParams P) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  uint8_t* ring = dsm;
+  Smem<S>& sm = *reinterpret_cast<Smem<S>*>(dsm + (size_t)S::NST * S::STB);
+  for (int i = threadIdx.x; i < S::NOFF; i += blockDim.x) sm.wtab[i] = P.w[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::NST; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kConsumerWarps);
+    }
+    sm.abort_flag = 0;
+    sm.tokens_done = 0;
+    sm.wait_hop_ns = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int cta = blockIdx.x;
+  if (threadIdx.x >= kConsumerThreads) producer<S>(P, sm, ring, cta);
+  else consumers<S>(P, sm, ring, cta);
+}
+
+template <class S>
+constexpr size_t smem_bytes() { return (size_t)S::NST * S::STB + sizeof(Smem<S>); }
+
+}  // namespace mk
