@@ -132,6 +132,7 @@ struct Smem {
   volatile int tokens_done;
   unsigned long long wait_hop_ns;     // trace accounting (thread 0)
   const __nv_bfloat16* wtab[S::NOFF]; // weight pointer table (offsets order)
+  KParams prm;                        // copy of the launch parameters
   alignas(8) uint64_t full[S::NST];
   alignas(8) uint64_t empty[S::NST];
 };
@@ -162,14 +163,33 @@ struct Spin {
   }
 };
 
+// Slow paths of the waits live out of line: the fast path (already complete)
+// stays a couple of instructions at every call site, which keeps the kernel's
+// hot loop small enough for the instruction caches.
 template <class S>
-__device__ __forceinline__ bool wait_bar(const KParams& P, Smem<S>& sm, uint64_t* bar, uint32_t parity) {
-  if (mbar_test(bar, parity)) return true;
+__device__ __noinline__ bool wait_bar_slow(const KParams& P, Smem<S>& sm, uint64_t* bar, uint32_t parity) {
   Spin sp;
   while (!mbar_try_wait(bar, parity)) {
     if (!sp.keep_going(P, sm)) return false;
   }
   return true;
+}
+template <class S>
+__device__ __forceinline__ bool wait_bar(const KParams& P, Smem<S>& sm, uint64_t* bar, uint32_t parity) {
+  if (mbar_test(bar, parity)) return true;
+  return wait_bar_slow(P, sm, bar, parity);
+}
+// Re-poll one tagged word until it carries `tag` (bounded); returns the word.
+template <class S>
+__device__ __noinline__ uint64_t poll_tagged_slow(const KParams& P, Smem<S>& sm, const uint64_t* src,
+                                                  uint32_t tag) {
+  uint64_t v;
+  Spin sp;
+  do {
+    v = ld_relaxed(src);
+    if ((uint32_t)(v >> 32) == tag) break;
+  } while (sp.keep_going(P, sm));
+  return v;
 }
 
 // ---- per-step plan shared by producer and consumers -------------------------
@@ -205,122 +225,133 @@ __device__ __forceinline__ size_t kv_index(int l, int kind, int h, int pos, int 
 namespace mk {
 
 // ---- producer ---------------------------------------------------------------
+// The copy issuer, one thread.  Its methods stay out of line so the kernel's
+// code (shared instruction caches with the consumer warps) stays small.
 template <class S>
-__device__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ring, int cta) {
-  if ((threadIdx.x & 31) != 0) return;
-  const int N = P.ncta;
-  const uint32_t nst = (uint32_t)P.nst;
-  const uint64_t pol = policy_evict_first();
-  uint32_t k = 0;
+struct Producer {
+  const KParams* P;
+  Smem<S>* sm;
+  uint8_t* ring;
+  uint64_t pol;
+  uint32_t nst;
+  uint32_t k = 0;   // stages issued so far
   bool ok = true;
 
-  auto acquire = [&](uint32_t& slot) -> bool {
+  __device__ __noinline__ bool acquire(uint32_t& slot) {
     slot = k % nst;
     const uint32_t ph = (k / nst) & 1u;
-    if (!wait_bar(P, sm, &sm.empty[slot], ph ^ 1u)) { ok = false; return false; }
-    return true;
-  };
+    if (!wait_bar(*P, *sm, &sm->empty[slot], ph ^ 1u)) ok = false;
+    return ok;
+  }
   // Contiguous bytes (LM-head rows, cached K/V): one copy per stage.
-  auto issue = [&](const void* src, uint32_t bytes) {
+  __device__ __noinline__ void issue(const void* src, uint32_t bytes) {
     uint32_t slot;
     if (!ok || !acquire(slot)) return;
-    mbar_arrive_expect_tx(&sm.full[slot], bytes);
-    bulk_g2s(ring + (size_t)slot * S::STB, src, bytes, &sm.full[slot], pol);
+    mbar_arrive_expect_tx(&sm->full[slot], bytes);
+    bulk_g2s(ring + (size_t)slot * S::STB, src, bytes, &sm->full[slot], pol);
     ++k;
-  };
-  auto issue_rows = [&](const __nv_bfloat16* base, int r0, int r1, int K) {
+  }
+  __device__ __noinline__ void rows(const __nv_bfloat16* base, int r0, int r1, int K) {
     const int rpc = S::STB / (2 * K);
     for (int r = r0; r < r1 && ok; r += rpc) {
       const int n = min(rpc, r1 - r);
       issue(base + (size_t)r * K, (uint32_t)(n * 2 * K));
     }
-  };
+  }
   // Rows for the tensor-core GEMV: one copy per row, at pitch 2K + 16.
-  auto issue_rows_padded = [&](const __nv_bfloat16* base, int r0, int r1, int K) {
+  __device__ __noinline__ void rows_padded(const __nv_bfloat16* base, int r0, int r1, int K) {
     const int pitch = 2 * K + kRowPad;
     const int rpc = S::STB / pitch;
     for (int r = r0; r < r1 && ok; r += rpc) {
       const int n = min(rpc, r1 - r);
       uint32_t slot;
       if (!acquire(slot)) return;
-      mbar_arrive_expect_tx(&sm.full[slot], (uint32_t)(n * 2 * K));
+      mbar_arrive_expect_tx(&sm->full[slot], (uint32_t)(n * 2 * K));
       for (int i = 0; i < n; ++i)
         bulk_g2s(ring + (size_t)slot * S::STB + (size_t)i * pitch, base + (size_t)(r + i) * K,
-                 (uint32_t)(2 * K), &sm.full[slot], pol);
+                 (uint32_t)(2 * K), &sm->full[slot], pol);
       ++k;
     }
-  };
-
-  for (int t = 0; t < P.n_steps && ok; ++t) {
-    const int p = P.pos0 + t;
-    const int nc = chunks_per_head<S>(p);
-    const int nitems = S::NKV * nc;
-    for (int l = 0; l < S::L && ok; ++l) {
-      trace_point<S>(P, t, cta, 7 * l);
-      {
-        int s0, s1;
-        split_rows(S::QKV, N, cta, phase_rot(l, 0, N), s0, s1);
-#pragma unroll
-        for (int m = 0; m < 3; ++m) {
-          int a, b, o;
-          if (qkv_part<S>(s0, s1, m, a, b, o)) issue_rows_padded(wptr(l, W_Q + m), a, b, S::H);
-        }
-      }
-      // Cached K/V of this CTA's attention items.  Positions < p-1 were
-      // written by steps <= t-2 of this launch (or earlier launches); wait
-      // until the consumers have finished step t-2 before reading them.
-      // Position p-1 is read by the consumers directly (written by step t-1).
-      int ilo, ihi;
-      items_of_cta(cta, l, nitems, N, ilo, ihi);
-      for (int i = ilo; i < ihi && ok; ++i) {
-        const int h = i / nc, j = i % nc;
-        int c0, c1;
-        chunk_range(p, nc, j, c0, c1);
-        const int te = min(c1, p - 1);
-        if (c0 >= te) continue;
-        if (t >= 2) {
-          Spin sp;
-          while (sm.tokens_done < t - 1) {
-            if (!sp.keep_going(P, sm)) { ok = false; break; }
-          }
-          if (!ok) break;
-          fence_proxy_async_global();
-        }
-        for (int a = c0; a < te && ok; a += S::SUBP) {
-          const int n = min(S::SUBP, te - a);
-          issue(P.kv + kv_index<S>(l, 0, h, a, P.max_seq), (uint32_t)(n * S::D * 2));
-          issue(P.kv + kv_index<S>(l, 1, h, a, P.max_seq), (uint32_t)(n * S::D * 2));
-        }
-      }
-      int r0, r1;
-      MK_DP(24);
-      split_rows(S::H, N, cta, phase_rot(l, 1, N), r0, r1);
-      issue_rows_padded(wptr(l, W_O), r0, r1, S::Q);
-      MK_DP(25);
-      split_rows(S::I, N, cta, phase_rot(l, 2, N), r0, r1);
-      issue_rows_padded(wptr(l, W_GATE), r0, r1, S::H);
-      MK_DP(26);
-      issue_rows_padded(wptr(l, W_UP), r0, r1, S::H);
-      MK_DP(27);
-      split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
-      issue_rows_padded(wptr(l, W_DOWN), r0, r1, S::I);
-      MK_DP(28);
-    }
-    int r0, r1;
-    split_rows(S::V, N, cta, phase_rot(S::L, 4, N), r0, r1);
-    issue_rows(sm.wtab[0], r0, r1, S::H);
   }
-  if (!ok) {
-    // Abandoned: wait (bounded) for the copies already in flight so that no
-    // bulk copy lands in shared memory after this CTA has exited.
+  // Cached K/V of attention items [ilo, ihi) of layer l at step t.  Positions
+  // < p-1 were written by steps <= t-2 of this launch (or earlier launches):
+  // wait until the consumers have finished step t-2 before reading them.
+  // Position p-1 is read by the consumers directly (written by step t-1).
+  __device__ __noinline__ void kv_items(int t, int l, int p, int nc, int ilo, int ihi) {
+    for (int i = ilo; i < ihi && ok; ++i) {
+      const int h = i / nc, j = i % nc;
+      int c0, c1;
+      chunk_range(p, nc, j, c0, c1);
+      const int te = min(c1, p - 1);
+      if (c0 >= te) continue;
+      if (t >= 2) {
+        Spin sp;
+        while (sm->tokens_done < t - 1) {
+          if (!sp.keep_going(*P, *sm)) { ok = false; return; }
+        }
+        fence_proxy_async_global();
+      }
+      for (int a = c0; a < te && ok; a += S::SUBP) {
+        const int n = min(S::SUBP, te - a);
+        issue(P->kv + kv_index<S>(l, 0, h, a, P->max_seq), (uint32_t)(n * S::D * 2));
+        issue(P->kv + kv_index<S>(l, 1, h, a, P->max_seq), (uint32_t)(n * S::D * 2));
+      }
+    }
+  }
+  // Abandoned: wait (bounded) for the copies already in flight so that no
+  // bulk copy lands in shared memory after this CTA has exited.
+  __device__ __noinline__ void drain() {
     const uint32_t first = k > nst ? k - nst : 0;
     for (uint32_t c = first; c < k; ++c) {
       const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(&sm.full[c % nst], (c / nst) & 1u)) {
-        if ((long long)(globaltimer_ns() - t0) > P.timeout_ns) break;
+      while (!mbar_try_wait(&sm->full[c % nst], (c / nst) & 1u)) {
+        if ((long long)(globaltimer_ns() - t0) > P->timeout_ns) break;
       }
     }
   }
+};
+
+template <class S>
+__device__ __noinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ring, int cta) {
+  if ((threadIdx.x & 31) != 0) return;
+  const int N = P.ncta;
+  Producer<S> pr;
+  pr.P = &P;
+  pr.sm = &sm;
+  pr.ring = ring;
+  pr.pol = policy_evict_first();
+  pr.nst = (uint32_t)P.nst;
+#pragma unroll 1
+  for (int t = 0; t < P.n_steps && pr.ok; ++t) {
+    const int p = P.pos0 + t;
+    const int nc = chunks_per_head<S>(p);
+    const int nitems = S::NKV * nc;
+#pragma unroll 1
+    for (int l = 0; l < S::L && pr.ok; ++l) {
+      trace_point<S>(P, t, cta, 7 * l);
+      int r0, r1;
+      split_rows(S::QKV, N, cta, phase_rot(l, 0, N), r0, r1);
+#pragma unroll 1
+      for (int m = 0; m < 3; ++m) {
+        int a, b, o;
+        if (qkv_part<S>(r0, r1, m, a, b, o)) pr.rows_padded(wptr(l, W_Q + m), a, b, S::H);
+      }
+      int ilo, ihi;
+      items_of_cta(cta, l, nitems, N, ilo, ihi);
+      pr.kv_items(t, l, p, nc, ilo, ihi);
+      split_rows(S::H, N, cta, phase_rot(l, 1, N), r0, r1);
+      pr.rows_padded(wptr(l, W_O), r0, r1, S::Q);
+      split_rows(S::I, N, cta, phase_rot(l, 2, N), r0, r1);
+      pr.rows_padded(wptr(l, W_GATE), r0, r1, S::H);
+      pr.rows_padded(wptr(l, W_UP), r0, r1, S::H);
+      split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
+      pr.rows_padded(wptr(l, W_DOWN), r0, r1, S::I);
+    }
+    int r0, r1;
+    split_rows(S::V, N, cta, phase_rot(S::L, 4, N), r0, r1);
+    pr.rows(sm.wtab[0], r0, r1, S::H);
+  }
+  if (!pr.ok) pr.drain();
 }
 
 }  // namespace mk
@@ -334,7 +365,7 @@ namespace mk {
 // kBatch in flight) and only then checks tags, so a hop costs about one L2
 // round trip instead of one per word.  No barrier inside.
 template <class S>
-__device__ __forceinline__ void wait_tagged(const KParams& P, Smem<S>& sm, const uint64_t* src,
+__device__ __noinline__ void wait_tagged(const KParams& P, Smem<S>& sm, const uint64_t* src,
                                             int n, uint32_t tag, float* dst) {
   constexpr int kBatch = 8;
   const uint64_t tw0 = (P.trace != nullptr && threadIdx.x == 0) ? globaltimer_ns() : 0;
@@ -349,13 +380,7 @@ __device__ __forceinline__ void wait_tagged(const KParams& P, Smem<S>& sm, const
     for (int k = 0; k < kBatch; ++k) {
       const int i = base + k * kConsumerThreads;
       if (i >= n) break;
-      if ((uint32_t)(v[k] >> 32) != tag) {
-        Spin sp;
-        do {
-          if (!sp.keep_going(P, sm)) break;
-          v[k] = ld_relaxed(src + i);
-        } while ((uint32_t)(v[k] >> 32) != tag);
-      }
+      if ((uint32_t)(v[k] >> 32) != tag) v[k] = poll_tagged_slow(P, sm, src + i, tag);
       dst[i] = __uint_as_float((uint32_t)v[k]);
     }
   }
@@ -367,13 +392,7 @@ template <class S>
 __device__ __forceinline__ float wait_word(const KParams& P, Smem<S>& sm, const uint64_t* src,
                                            uint32_t tag) {
   uint64_t v = ld_relaxed(src);
-  if ((uint32_t)(v >> 32) != tag) {
-    Spin sp;
-    do {
-      if (!sp.keep_going(P, sm)) break;
-      v = ld_relaxed(src);
-    } while ((uint32_t)(v >> 32) != tag);
-  }
+  if ((uint32_t)(v >> 32) != tag) v = poll_tagged_slow(P, sm, src, tag);
   return __uint_as_float((uint32_t)v);
 }
 
@@ -404,7 +423,7 @@ __device__ __forceinline__ void split_one(Smem<S>& sm, int i, float x) {
   sm.xs[2][i] = __float2bfloat16_rn(r2);
 }
 template <class S>
-__device__ __forceinline__ void split_xin(Smem<S>& sm, int n) {
+__device__ __noinline__ void split_xin(Smem<S>& sm, int n) {
   for (int i = threadIdx.x; i < n; i += kConsumerThreads) split_one(sm, i, sm.xin[i]);
   consumer_sync(kConsumerThreads);
 }
@@ -428,7 +447,7 @@ struct GainRegs {
 // split into xs.  Replaces rmsnorm_float_in (src/rmsnorm.cuh:87-108); computed
 // redundantly in every CTA and kept in shared memory, never written back.
 template <class S>
-__device__ __forceinline__ void rmsnorm_to_xin(Smem<S>& sm, const GainRegs<S>& gr) {
+__device__ __noinline__ void rmsnorm_to_xin(Smem<S>& sm, const GainRegs<S>& gr) {
   float ss = 0.f;
   for (int i = threadIdx.x; i < S::H; i += kConsumerThreads) ss += sm.xres[i] * sm.xres[i];
   ss = consumer_sum(sm, ss);
@@ -456,7 +475,7 @@ __device__ __forceinline__ void rmsnorm_to_xin(Smem<S>& sm, const GainRegs<S>& g
 // partial sums are added in a fixed order.  Up to 4 stages (<= 32 rows) are
 // consumed per group.  All consumer threads must call this.
 template <class S, int K>
-__device__ __forceinline__ void gemv_mma(const KParams& P, Smem<S>& sm, const uint8_t* ring,
+__device__ __noinline__ void gemv_mma(const KParams& P, Smem<S>& sm, const uint8_t* ring,
                                          uint32_t& kc, int r0, int r1, float* out) {
   constexpr int PITCH = S::template pitch<K>();
   constexpr int RPC = S::template rows_per_stage<K>();
@@ -536,7 +555,7 @@ __device__ __forceinline__ void gemv_mma(const KParams& P, Smem<S>& sm, const ui
 // lm_head_argmax_phase1 (src/sampling.cuh:32-89): a warp reads whole 2*H-byte
 // rows from shared memory instead of one thread walking each row.
 template <class S>
-__device__ __forceinline__ void lm_rows(const KParams& P, Smem<S>& sm, const uint8_t* ring,
+__device__ __noinline__ void lm_rows(const KParams& P, Smem<S>& sm, const uint8_t* ring,
                                         uint32_t& kc, int r0, int r1, float* logits_row0,
                                         float& best_v, int& best_i) {
   constexpr int PPR = S::H / 256;
@@ -583,7 +602,7 @@ namespace mk {
 // PV: thread (part, g, d) sums positions = part (mod parts).  The running
 // (m, l) live in sm.mrun/lrun; the PV accumulator stays in `acc`.
 template <class S>
-__device__ __forceinline__ void attend_block(Smem<S>& sm, const __nv_bfloat16* K,
+__device__ __noinline__ void attend_block(Smem<S>& sm, const __nv_bfloat16* K,
                                              const __nv_bfloat16* V, int n, float& acc) {
   constexpr int D = S::D, GRP = S::GRP;
   constexpr int EPL = D / 32;  // elements per lane
@@ -650,7 +669,7 @@ __device__ __forceinline__ void attend_block(Smem<S>& sm, const __nv_bfloat16* K
 // (src/rmsnorm.cuh:57-84), apply_rope_inplace (src/attention.cuh:22-44),
 // append_kv (src/kv_cache.cuh:58-78) and warp_attention (src/attention.cuh:100-167).
 template <class S>
-__device__ void attention_item(const KParams& P, Smem<S>& sm, const uint8_t* ring, uint32_t& kc,
+__device__ __noinline__ void attention_item(const KParams& P, Smem<S>& sm, const uint8_t* ring, uint32_t& kc,
                                int t, int l, int p, uint32_t seq, int h, int j, int nc, int item) {
   constexpr int D = S::D, GRP = S::GRP, HALF = D / 2;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -789,7 +808,7 @@ __device__ void attention_item(const KParams& P, Smem<S>& sm, const uint8_t* rin
 // of two chunks' {m, l, acc} at a time, so short contexts (nc <= 2) cost one
 // L2 round trip.  Also writes the bf16 split terms of each output.
 template <class S>
-__device__ __forceinline__ void merge_attention(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc) {
+__device__ __noinline__ void merge_attention(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc) {
   constexpr int D = S::D, GRP = S::GRP;
   constexpr int EPT = S::Q >= kConsumerThreads ? S::Q / kConsumerThreads : 1;
   static_assert(D % EPT == 0, "a thread's outputs stay inside one head");
@@ -846,10 +865,11 @@ __device__ __forceinline__ void merge_attention(const KParams& P, Smem<S>& sm, i
 namespace mk {
 
 template <class S>
-__device__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, int cta) {
+__device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, int cta) {
   const int N = P.ncta, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint32_t kc = 0;
   int tok = P.forced[0];
+  #pragma unroll 1
   for (int t = 0; t < P.n_steps; ++t) {
     const int p = P.pos0 + t;
     const uint32_t seq = P.seq0 + (uint32_t)t;
@@ -861,6 +881,7 @@ __device__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, in
       for (int i = tid; i < S::H; i += kConsumerThreads) sm.xres[i] = __bfloat162float(er[i]);
     }
     consumer_sync(kConsumerThreads);
+    #pragma unroll 1
     for (int l = 0; l < S::L; ++l) {
       // ---- P1: x -> RMSNorm -> q, k, v rows --------------------------------
       GainRegs<S> gains;
@@ -875,7 +896,7 @@ __device__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, in
       {
         int s0, s1;
         split_rows(S::QKV, N, cta, phase_rot(l, 0, N), s0, s1);
-#pragma unroll
+#pragma unroll 1
         for (int m = 0; m < 3; ++m) {
           int a, b, o;
           if (qkv_part<S>(s0, s1, m, a, b, o))
@@ -1037,6 +1058,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   uint8_t* ring = dsm;
   Smem<S>& sm = *reinterpret_cast<Smem<S>*>(dsm + (size_t)S::NST * S::STB);
   for (int i = threadIdx.x; i < S::NOFF; i += blockDim.x) sm.wtab[i] = P.w[i];
+  if (threadIdx.x == 0) sm.prm = P;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::NST; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -1049,8 +1071,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   }
   __syncthreads();
   const int cta = blockIdx.x;
-  if (threadIdx.x >= kConsumerThreads) producer<S>(P, sm, ring, cta);
-  else consumers<S>(P, sm, ring, cta);
+  // Out-of-line device functions read the parameters from shared memory.
+  if (threadIdx.x >= kConsumerThreads) producer<S>(sm.prm, sm, ring, cta);
+  else consumers<S>(sm.prm, sm, ring, cta);
 }
 
 template <class S>

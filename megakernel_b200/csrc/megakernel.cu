@@ -86,8 +86,9 @@ void host_rope(int D, double theta, int positions, float* c, float* s) {
   for (int i = 0; i < half; ++i) {
     // inv_freq = 1 / theta^(2i/D) in fp32, angle = inv_freq * pos in fp32
     // (transformers modeling_rope_utils.py:178, modeling_qwen3.py:140-144).
+    // torch evaluates theta ** x like a double pow rounded to fp32.
     const float expo = (float)(2 * i) / (float)D;
-    const float inv = 1.0f / powf((float)theta, expo);
+    const float inv = 1.0f / (float)pow(theta, (double)expo);
     for (int p = 0; p < positions; ++p) {
       const float ang = (float)p * inv;
       c[(size_t)p * half + i] = (float)cos((double)ang);
