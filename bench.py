@@ -1,0 +1,283 @@
+"""Benchmark: batch-1 greedy decode of the Qwen3-0.6B (head_dim 64) shape.
+
+Workload: seeded random-init weights, a 128-token
+uniform-random prompt (seed 1), greedy decode of 512 tokens.  One "step" is
+one kernel launch that decodes those 512 tokens from position 128 (the
+prompt's KV prefix is prefilled once, untimed, and every step restarts from
+it).  `value` = generated tokens / device time (CUDA events on the launching
+stream), inputs resident in HBM; the weights (972 MB) exceed the 126 MB L2,
+so no flush is needed between steps.
+
+Multi-GPU (`torchrun --nproc-per-node N`): the path does not shard at batch
+1 without communication, so each rank runs an independent replica of the
+workload on its own GPU ("replicas only", weak scaling); value = all ranks'
+tokens / max-over-ranks time.
+
+`--impl reference` times the reference's own path for this workload: HF
+Qwen3ForCausalLM.generate in bf16 on the host cores (host/validate.py:40-52),
+rank 0 only, on a bounded sample (see cpu_baseline).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s, Qwen3-0.6B shape, B=1 on 1×B200; % of HBM roofline"
+PROMPT, GEN = 128, 512
+# DRAM bytes (read + write) per decoded token of the decode kernel, from the
+# ncu capture summarised in profiles/decode_kernel_d64_b1.md (8-step launch
+# at position 128, scaled per token); None until measured.
+NCU_TRAFFIC_PER_TOKEN = None
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        sm = [float(r[0]) for r in self.rows if r and r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if len(r) > 1 and r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > i + 2 and r[i + 2].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_reference(shape, w, prompt, n_new=12, threads=None):
+    """HF bf16 greedy generate on the host cores; returns (tok/s, cores, sample)."""
+    from oracle.hf_reference import build_hf_model, hf_generate
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = build_hf_model(shape, w, torch.bfloat16)
+    hf_generate(model, prompt[:8], 2)  # warm up
+    t0 = time.perf_counter()
+    hf_generate(model, prompt, 1)
+    t_prefill = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    hf_generate(model, prompt, n_new + 1)
+    t_all = time.perf_counter() - t0
+    tps = n_new / max(t_all - t_prefill, 1e-9)
+    sample = (f"HF Qwen3ForCausalLM.generate bf16 (host/validate.py:40-52 path), {PROMPT}-token prompt, "
+              f"{n_new} greedy tokens timed (prefill subtracted), torch threads={threads}")
+    return tps, threads, sample
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from megakernel_b200 import weights as W
+    from megakernel_b200.shapes import QWEN3_0_6B_D64 as shape
+    w = W.random_weights(shape, 0)
+    prompt = W.prompt_ids(shape, PROMPT, seed=1)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        tps, cores, sample = cpu_reference(shape, w, prompt, n_new=args.ref_tokens)
+        if i >= args.warmup:
+            vals.append(tps)
+    v = statistics.median(vals)
+    line = {"metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config_dict(args.gpus),
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(n):
+    return {"workload": "configs[1]: Qwen3-0.6B-shaped (head_dim 64, intermediate 2816), B=1, "
+                        f"{PROMPT}-token random prompt, {GEN} greedy tokens per GPU",
+            "model": "qwen3-0.6b-d64 (random init, seed 0)", "global_batch": n,
+            "seq_len": PROMPT + GEN, "parallelism": f"replicas x{n}" if n > 1 else "single",
+            "l2_policy": "inputs larger than L2 (972 MB of weights streamed per token)"}
+
+
+def run_ours(args, world, rank, local):
+    from megakernel_b200 import weights as W
+    from megakernel_b200.bridge import MegakernelEngine
+    from megakernel_b200.shapes import QWEN3_0_6B_D64 as shape
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w = W.random_weights(shape, 0)
+    flat, offs = W.flat_bytes(shape, w)
+    eng = MegakernelEngine(flat=flat, offsets=offs, shape=shape, device=local, max_seq=PROMPT + GEN + 8)
+    prompt = W.prompt_ids(shape, PROMPT, seed=1)
+    stream = torch.cuda.Stream(dev)
+    ptoks = torch.tensor(prompt, dtype=torch.int32, device=dev)
+    pout = torch.zeros(PROMPT, dtype=torch.int32, device=dev)
+    eng.decode_n(ptoks, PROMPT, pout)            # prefill once (token-serial, untimed)
+    first = pout[PROMPT - 1:PROMPT].clone()
+    out = torch.zeros(GEN, dtype=torch.int32, device=dev)
+
+    def step():
+        eng.set_pos(PROMPT)
+        eng.decode_n(first, 1, out, n_steps=GEN, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        for s, e in ev:
+            s.record(stream)
+            step()
+            e.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    per = [s.elapsed_time(e) for s, e in ev]
+    ms_total = max_over_ranks(sum(per), world, dev)
+    ms_step = ms_total / args.steps
+    tokens = GEN * args.steps * world
+    value = tokens / (ms_total / 1e3)
+    # roofline of the dominant (only) kernel: algorithmic bytes per launch / launch time
+    bytes_launch = sum(shape.algorithmic_bytes(PROMPT + i) for i in range(GEN))
+    achieved = bytes_launch / (statistics.mean(per) / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    # end to end through the public C ABI with host buffers: prompt H2D,
+    # prefill + 512 greedy tokens in one call, tokens D2H
+    eng.reset()
+    eng.generate_ids(prompt, 8)
+    e2e_times = []
+    for _ in range(max(1, min(args.steps, 3))):
+        eng.reset()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        res = eng.generate_ids(prompt, GEN)
+        e2e_times.append(time.perf_counter() - t0)
+    e2e_wall = max_over_ranks(statistics.median(e2e_times), world, dev)
+    check = out.cpu().tolist()
+    assert res == [int(first.item())] + check[:GEN - 1], "e2e and device paths disagree"
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, cores, sample = cpu_reference(shape, w, prompt, n_new=args.ref_tokens)
+        cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample}
+    traffic = NCU_TRAFFIC_PER_TOKEN * GEN if NCU_TRAFFIC_PER_TOKEN else None
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 weights/KV, fp32 activations+accumulate", "data": "synthetic",
+        "config": config_dict(world),
+        "tok_per_s_per_gpu": value / world, "us_per_token": ms_step * 1e3 / GEN,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "frac_of_8TBs_spec": achieved / 8000.0, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": bytes_launch},
+        "e2e": {"value": GEN * world / e2e_wall, "unit": "tok/s",
+                "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": GEN * 4,
+                "note": "megakernel_generate with host buffers: prompt copy-in, token-serial prefill "
+                        f"of {PROMPT} tokens + {GEN} greedy tokens, copy-out; wall clock"},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-tokens", type=int, default=12)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
