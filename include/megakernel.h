@@ -117,6 +117,31 @@ int megakernel_trace_points(void* handle);
  * (needs megakernel_set_trace active; NULL turns it off). */
 int megakernel_set_trace_detail(void* handle, void* d_buf);
 
+/* ---- decode without device allocation ------------------------------------ */
+
+#define MK_NOALLOC_MAX_POS 2048           /* pos + n_steps must not exceed this */
+#define MK_NOALLOC_SCRATCH_BYTES 781056   /* static device scratch per GPU */
+
+/* No counterpart in the reference.  For callers that cannot allocate device
+ * memory (a runtime that owns all device allocations, an allocator-free
+ * loader, a plugin that must keep its footprint fixed): runs n_steps decode
+ * steps of the graded shape (head_dim 64, intermediate 2816) like
+ * megakernel_decode_n, but on caller-owned buffers only -- weights + offsets
+ * as for megakernel_init, the KV cache d_kv ([layers, 2, kv_heads,
+ * kv_max_seq, head_dim] bf16) starting at position pos, tokens in/out and
+ * optional logits -- and calls no cudaMalloc/cudaFree.  Its scratch is a
+ * fixed MK_NOALLOC_SCRATCH_BYTES array in the library's device image, held
+ * on every GPU that loads the library until exit.  pos + n_steps beyond
+ * MK_NOALLOC_MAX_POS or kv_max_seq returns MK_ERR_CAPACITY.  The first call
+ * on a device (the current one) sets that device up with blocking copies:
+ * make it before any stream capture.  All calls share the scratch, so calls
+ * that overlap on the GPU race.  Blocks until done; returns MK_OK or an
+ * MK_ERR_* code.  The caller tracks the position (pos += n_steps). */
+int megakernel_decode_noalloc(const void* d_weights, const long long* offsets, int num_offsets,
+                              void* d_kv, int kv_max_seq, int pos, const int* d_tokens,
+                              int n_forced, int n_steps, int* d_out, float* d_logits,
+                              void* stream);
+
 /* ---- host-only helpers (no GPU needed) ----------------------------------- */
 
 /* Shape id matching a flat-binary offsets array, or MK_ERR_SHAPE. */

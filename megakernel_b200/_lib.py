@@ -15,7 +15,8 @@ ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libmegakernel.so")
 HEADER = os.path.join(ROOT, "include", "megakernel.h")
-SOURCES = [os.path.join(CSRC, f) for f in ("megakernel.cu", "decode_kernel.cuh", "ptx.cuh", "shapes.cuh")]
+SOURCES = [os.path.join(CSRC, f) for f in ("megakernel.cu", "noalloc.cu", "decode_kernel.cuh", "ptx.cuh",
+                                                  "shapes.cuh")]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
               "-shared", "-Xcompiler", "-fPIC"]
@@ -87,6 +88,8 @@ def signatures() -> dict:
         "megakernel_set_trace": ([vp, vp, c_int], c_int),
         "megakernel_trace_points": ([vp], c_int),
         "megakernel_set_trace_detail": ([vp, vp], c_int),
+        "megakernel_decode_noalloc": ([vp, llp, c_int, vp, c_int, c_int, vp, c_int, c_int, vp, vp, vp],
+                                      c_int),
         "megakernel_infer_shape": ([llp, c_int], c_int),
         "megakernel_rope_table": ([c_int, ctypes.c_double, c_int, fp, fp], c_int),
         "megakernel_plan_bytes": ([c_int, c_int, c_int, llp], c_int),

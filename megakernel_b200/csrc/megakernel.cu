@@ -573,3 +573,7 @@ int megakernel_plan_bytes(int shape_id, int num_ctas, int pos, long long* bytes_
 }
 
 }  // extern "C"
+
+// The allocation-free entry point lives in its own file; it is compiled in
+// this translation unit so both entry points launch the same kernel image.
+#include "noalloc.cu"
