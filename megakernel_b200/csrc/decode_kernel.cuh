@@ -7,13 +7,13 @@
 // argmax -> next input token) without returning to the host.
 //
 // Structure of a CTA:
-//   * warp 16 (producer): walks this CTA's byte stream for every step --
+//   * warp 8 (producer): walks this CTA's byte stream for every step --
 //     its rows of each weight matrix and its share of the cached K/V -- and
 //     issues 1-D TMA bulk copies into a ring of shared-memory stages, each
 //     completing on a "full" mbarrier.  Weights do not depend on activations,
 //     so the producer runs ahead of the math by up to the ring size, through
 //     every inter-CTA dependency, keeping HBM busy.
-//   * warps 0-15 (consumers): per phase, wait for the activation vector the
+//   * warps 0-7 (consumers): per phase, wait for the activation vector the
 //     phase needs, then do the math on ring stages and release them on an
 //     "empty" mbarrier.
 //
@@ -27,6 +27,15 @@
 #pragma once
 #include "ptx.cuh"
 #include "shapes.cuh"
+
+// Phase functions are inlined into the consumer loop (measured faster than
+// out-of-line calls, whose register save/restore goes through local memory);
+// MK_INLINE_PHASES=0 keeps them out of line for code-size experiments.
+#if defined(MK_INLINE_PHASES) && !MK_INLINE_PHASES
+#define MK_PHASE __noinline__
+#else
+#define MK_PHASE __forceinline__
+#endif
 
 namespace mk {
 
@@ -115,16 +124,17 @@ struct Smem {
   // term keeps 8 mantissa bits, together the 24 of fp32); padded rows keep
   // the three arrays in different banks.
   alignas(16) __nv_bfloat16 xs[3][S::XIN + 8];
-  float partw[kConsumerWarps][32];    // per-warp row partials of one GEMV group
+  float partw[kConsumerWarps][64];    // per-warp row partials of one GEMV pass (<= 4 tiles)
   float rowsum[2][kRowsMax];          // GEMV results of this CTA's rows
-  float qs[S::GRP][S::D];             // normed + roped queries of one KV head
-  float sc[S::GRP][S::SUBP];          // scores / probabilities of one block
+  alignas(16) float qs[S::GRP][S::D];     // normed + roped queries (read as float4)
+  float sc[S::GRP][S::SUBP + 2];      // scores / probabilities of one block
   float pv[kConsumerThreads];         // PV partials (parts x GRP x D)
   float mrun[S::GRP], lrun[S::GRP], corr[S::GRP];
   float gq[S::D], gk[S::D];           // q_norm / k_norm gains of the layer
   float rc[S::D / 2], rs[S::D / 2];   // RoPE cos / sin row of position p
-  __nv_bfloat16 kx[2][S::D];          // K rows not in the ring (prev + current)
-  __nv_bfloat16 vx[2][S::D];
+  // K/V rows not in the ring (prev + current); read with 16-byte loads.
+  alignas(16) __nv_bfloat16 kx[2][S::D];
+  alignas(16) __nv_bfloat16 vx[2][S::D];
   float red[kConsumerWarps * 2];
   int redi[kConsumerWarps];
   int next_token;
@@ -133,6 +143,7 @@ struct Smem {
   unsigned long long wait_hop_ns;     // trace accounting (thread 0)
   const __nv_bfloat16* wtab[S::NOFF]; // weight pointer table (offsets order)
   KParams prm;                        // copy of the launch parameters
+  alignas(8) unsigned char prod[64];  // the producer's state (see Producer)
   alignas(8) uint64_t full[S::NST];
   alignas(8) uint64_t empty[S::NST];
 };
@@ -234,8 +245,8 @@ struct Producer {
   uint8_t* ring;
   uint64_t pol;
   uint32_t nst;
-  uint32_t k = 0;   // stages issued so far
-  bool ok = true;
+  uint32_t k;       // stages issued so far
+  bool ok;
 
   __device__ __noinline__ bool acquire(uint32_t& slot) {
     slot = k % nst;
@@ -315,7 +326,12 @@ template <class S>
 __device__ __noinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ring, int cta) {
   if ((threadIdx.x & 31) != 0) return;
   const int N = P.ncta;
-  Producer<S> pr;
+  // Its state lives in shared memory: the methods take `this`, and a stack
+  // object would be local memory, which misses the nearly absent L1.
+  static_assert(sizeof(Producer<S>) <= sizeof(sm.prod), "producer state");
+  Producer<S>& pr = *reinterpret_cast<Producer<S>*>(sm.prod);
+  pr.k = 0;
+  pr.ok = true;
   pr.P = &P;
   pr.sm = &sm;
   pr.ring = ring;
@@ -365,9 +381,9 @@ namespace mk {
 // kBatch in flight) and only then checks tags, so a hop costs about one L2
 // round trip instead of one per word.  No barrier inside.
 template <class S>
-__device__ __noinline__ void wait_tagged(const KParams& P, Smem<S>& sm, const uint64_t* src,
+__device__ MK_PHASE void wait_tagged(const KParams& P, Smem<S>& sm, const uint64_t* src,
                                             int n, uint32_t tag, float* dst) {
-  constexpr int kBatch = 8;
+  constexpr int kBatch = 12;
   const uint64_t tw0 = (P.trace != nullptr && threadIdx.x == 0) ? globaltimer_ns() : 0;
   for (int base = threadIdx.x; base < n; base += kConsumerThreads * kBatch) {
     uint64_t v[kBatch];
@@ -423,7 +439,7 @@ __device__ __forceinline__ void split_one(Smem<S>& sm, int i, float x) {
   sm.xs[2][i] = __float2bfloat16_rn(r2);
 }
 template <class S>
-__device__ __noinline__ void split_xin(Smem<S>& sm, int n) {
+__device__ MK_PHASE void split_xin(Smem<S>& sm, int n) {
   for (int i = threadIdx.x; i < n; i += kConsumerThreads) split_one(sm, i, sm.xin[i]);
   consumer_sync(kConsumerThreads);
 }
@@ -447,7 +463,7 @@ struct GainRegs {
 // split into xs.  Replaces rmsnorm_float_in (src/rmsnorm.cuh:87-108); computed
 // redundantly in every CTA and kept in shared memory, never written back.
 template <class S>
-__device__ __noinline__ void rmsnorm_to_xin(Smem<S>& sm, const GainRegs<S>& gr) {
+__device__ MK_PHASE void rmsnorm_to_xin(Smem<S>& sm, const GainRegs<S>& gr) {
   float ss = 0.f;
   for (int i = threadIdx.x; i < S::H; i += kConsumerThreads) ss += sm.xres[i] * sm.xres[i];
   ss = consumer_sum(sm, ss);
@@ -464,70 +480,145 @@ __device__ __noinline__ void rmsnorm_to_xin(Smem<S>& sm, const GainRegs<S>& gr) 
   consumer_sync(kConsumerThreads);
 }
 
-// out[r - r0] = W[r, :] . x for rows [r0, r1) of a row-major bf16 matrix
-// with K columns, whose rows the producer placed in consecutive ring stages
-// at pitch 2K + 16.  Replaces gemv_block / gemv_qkv / gemv_gate_up_silu
-// (src/gemv.cuh:36-279) with warp-level tensor-core MMAs:
+// One tensor-core GEMV pass over up to three row segments that follow each
+// other in the ring (this CTA's rows of Wq, Wk, Wv; or of Wgate and Wup; or
+// of one matrix), all with K columns and the same input x:
+//     out_s[r] = scale * (W_s[r, :] . x).
+// The producer placed each segment's rows in consecutive stages at pitch
+// 2K + 16 (RPC rows per stage).  Replaces gemv_block / gemv_qkv /
+// gemv_gate_up_silu (src/gemv.cuh:36-279) with warp-level tensor-core MMAs:
 //   A = 16 weight rows x 16 columns (ldmatrix from the stage),
-//   B = 16 columns x 8, whose columns 0..2 are the hi/mid/lo bf16 terms of x,
-//   so row r's dot product is D[r][0] + D[r][1] + D[r][2] in fp32.
-// Warp w takes the 16-column slices ks = w, w + 16, ...; the 16 warps'
-// partial sums are added in a fixed order.  Up to 4 stages (<= 32 rows) are
-// consumed per group.  All consumer threads must call this.
-template <class S, int K>
-__device__ __noinline__ void gemv_mma(const KParams& P, Smem<S>& sm, const uint8_t* ring,
-                                         uint32_t& kc, int r0, int r1, float* out) {
-  constexpr int PITCH = S::template pitch<K>();
-  constexpr int RPC = S::template rows_per_stage<K>();
-  static_assert(RPC >= 1, "stage too small");
-  constexpr int GCH0 = 32 / RPC;
-  constexpr int GCH = GCH0 < 1 ? 1 : (GCH0 > 4 ? 4 : GCH0);
-  constexpr int GROWS = GCH * RPC;                 // rows per group (<= 32)
-  static_assert(GROWS <= 32, "two 16-row tiles per group");
-  constexpr int KS = K / 16;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, tq = lane & 3;
-  const uint32_t nst = (uint32_t)P.nst;
-  const uint32_t* xs0 = reinterpret_cast<const uint32_t*>(&sm.xs[g < 3 ? g : 0][0]);
-  for (int g0 = r0; g0 < r1; g0 += GROWS) {
-    const int n = min(GROWS, r1 - g0);
-    const int nch = (n + RPC - 1) / RPC;
-    const uint32_t slot0 = kc % nst, ph0 = (kc / nst) & 1u;
-    bool ok = true;
+//   B = 16 columns x 8, whose columns 0..2 are the hi/mid/lo bf16 terms of x
+//       (sm.xs), so a row's dot product is D[r][0] + D[r][1] + D[r][2] in fp32.
+// Warp w takes the 16-column slices w, w + 8, ... of up to four 16-row tiles.
+//
+// The pass is split in two so that everything that does not depend on x runs
+// before the caller waits for x: prepare() waits for the stages, computes the
+// fragment addresses and loads the first PIT slices of weight fragments into
+// registers; finish() (after x is in sm.xs) runs the MMAs, reduces the 8
+// warps' partials in a fixed order and releases the stages.  Each segment has
+// <= 32 rows and the pass's stages fit the ring (checked on the host).  All
+// consumer threads call both; the plan lives in registers (inlined).
+template <class S, int K, int MAXT>
+struct GemvPlan {
+  static constexpr int PITCH = S::template pitch<K>();
+  static constexpr int RPC = S::template rows_per_stage<K>();
+  static constexpr int KS = K / 16;
+  static constexpr int ITER = KS / kConsumerWarps;
+  static constexpr int PIT = ITER < 2 ? ITER : 2;   // slices preloaded per tile
+  static_assert(RPC >= 1 && KS % kConsumerWarps == 0, "GEMV shape");
+  uint32_t slot0;
+  int nch, ntile, t0n, t1n, n0, n1, n2;
+  bool ok;
+  static_assert(MAXT >= 1 && MAXT <= 4, "tiles");
+  uint32_t abase[MAXT];
+  uint32_t pa[PIT][MAXT][4];
+
+  __device__ __forceinline__ void prepare(const KParams& P, Smem<S>& sm, const uint8_t* ring, uint32_t kc,
+                                          int m0, int m1, int m2) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t nst = (uint32_t)P.nst;
+    n0 = m0; n1 = m1; n2 = m2;
+    const int ch0 = (n0 + RPC - 1) / RPC, ch1 = (n1 + RPC - 1) / RPC, ch2 = (n2 + RPC - 1) / RPC;
+    nch = ch0 + ch1 + ch2;
+    t0n = (n0 + 15) >> 4;
+    t1n = (n1 + 15) >> 4;
+    ntile = t0n + t1n + ((n2 + 15) >> 4);
+    slot0 = kc % nst;
+    const uint32_t ph0 = (kc / nst) & 1u;
+    ok = true;
     for (int c = 0; c < nch; ++c) {
       uint32_t sl = slot0 + c, ph = ph0;
       if (sl >= nst) { sl -= nst; ph ^= 1u; }
-      ok = wait_bar(P, sm, &sm.full[sl], ph) && ok;
+      if (!mbar_test(&sm.full[sl], ph)) ok = wait_bar_slow(P, sm, &sm.full[sl], ph) && ok;
     }
     ok = __all_sync(0xffffffffu, ok);
 #pragma unroll
-    for (int tile = 0; tile < 2; ++tile) {
-      if (tile * 16 >= n) break;
-      // ldmatrix row pointer of this lane: matrices (rows 0-7 | 8-15) x (k 0-7 | 8-15).
-      int lrow = tile * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
-      if (lrow >= n) lrow = 0;  // rows past the segment: any valid address, result unused
-      const int c = lrow / RPC, rin = lrow - c * RPC;
+    for (int t = 0; t < MAXT; ++t) {
+      const bool in0 = t < t0n, in1 = !in0 && t < t0n + t1n;
+      const int tn = in0 ? n0 : (in1 ? n1 : n2);
+      const int tc = in0 ? 0 : (in1 ? ch0 : ch0 + ch1);
+      const int tr = in0 ? t * 16 : (in1 ? (t - t0n) * 16 : (t - t0n - t1n) * 16);
+      int lrow = tr + ((lane >> 3) & 1) * 8 + (lane & 7);
+      if (lrow >= tn) lrow = tr;  // rows past the segment: a valid address, result unused
+      const int c = tc + lrow / RPC, rin = lrow % RPC;
       uint32_t sl = slot0 + c;
       if (sl >= nst) sl -= nst;
-      const uint32_t abase =
-          smem_u32(ring + (size_t)sl * S::STB + (size_t)rin * PITCH) + (uint32_t)((lane >> 4) * 16);
-      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-      if (ok) {
-        for (int ks = warp; ks < KS; ks += kConsumerWarps) {
-          uint32_t a0, a1, a2, a3;
-          ldmatrix_x4(abase + ks * 32, a0, a1, a2, a3);
-          const uint32_t b0 = g < 3 ? xs0[(ks * 16 + 2 * tq) >> 1] : 0u;
-          const uint32_t b1 = g < 3 ? xs0[(ks * 16 + 2 * tq + 8) >> 1] : 0u;
-          mma_bf16_16816(d0, d1, d2, d3, a0, a1, a2, a3, b0, b1);
+      abase[t] = smem_u32(ring + (size_t)sl * S::STB + (size_t)rin * PITCH) + (uint32_t)((lane >> 4) * 16);
+    }
+    if (ok) {
+#pragma unroll
+      for (int it = 0; it < PIT; ++it)
+#pragma unroll
+        for (int t = 0; t < MAXT; ++t)
+          if (t < ntile)
+            ldmatrix_x4(abase[t] + (warp + it * kConsumerWarps) * 32, pa[it][t][0], pa[it][t][1],
+                        pa[it][t][2], pa[it][t][3]);
+    }
+  }
+
+  // scale: per-row factor applied to the dot products (the RMSNorm 1/rms when
+  // the caller passes x without it), or 1.
+  __device__ __forceinline__ uint32_t finish(const KParams& P, Smem<S>& sm, float* out0, float* out1,
+                                             float* out2, bool norm_scale) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tq = lane & 3;
+    const uint32_t nst = (uint32_t)P.nst;
+    if (nch == 0) return 0;
+    // Tile 0 alternates two accumulator sets so a single-tile pass (O,
+    // down) does not chain every MMA on the previous one.
+    float d[MAXT][4] = {}, e[4] = {};
+    if (ok) {
+      const uint32_t* xs0 = reinterpret_cast<const uint32_t*>(&sm.xs[g < 3 ? g : 0][0]);
+      // Preloaded slices first ...
+#pragma unroll
+      for (int it = 0; it < PIT; ++it) {
+        const int ks = warp + it * kConsumerWarps;
+        const uint32_t b0 = g < 3 ? xs0[ks * 8 + tq] : 0u;
+        const uint32_t b1 = g < 3 ? xs0[ks * 8 + tq + 4] : 0u;
+#pragma unroll
+        for (int t = 0; t < MAXT; ++t) {
+          if (t < ntile) {
+            if (t == 0 && (it & 1))
+              mma_bf16_16816(e[0], e[1], e[2], e[3], pa[it][t][0], pa[it][t][1], pa[it][t][2], pa[it][t][3], b0, b1);
+            else
+              mma_bf16_16816(d[t][0], d[t][1], d[t][2], d[t][3], pa[it][t][0], pa[it][t][1], pa[it][t][2],
+                             pa[it][t][3], b0, b1);
+          }
         }
       }
-      // Lane (g, tq=0) holds columns 0,1 of rows g, g+8; lane (g, tq=1) column 2.
-      float s0 = d0 + d1, s1 = d2 + d3;
-      s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-      if (tq == 0) {
-        sm.partw[warp][tile * 16 + g] = s0;
-        sm.partw[warp][tile * 16 + g + 8] = s1;
+      // ... then the rest, loaded from the stages as they are used.
+#pragma unroll 2
+      for (int it = PIT; it < ITER; ++it) {
+        const int ks = warp + it * kConsumerWarps;
+        const uint32_t b0 = g < 3 ? xs0[ks * 8 + tq] : 0u;
+        const uint32_t b1 = g < 3 ? xs0[ks * 8 + tq + 4] : 0u;
+#pragma unroll
+        for (int t = 0; t < MAXT; ++t) {
+          if (t < ntile) {
+            uint32_t a0, a1, a2, a3;
+            ldmatrix_x4(abase[t] + ks * 32, a0, a1, a2, a3);
+            if (t == 0 && (it & 1)) mma_bf16_16816(e[0], e[1], e[2], e[3], a0, a1, a2, a3, b0, b1);
+            else mma_bf16_16816(d[t][0], d[t][1], d[t][2], d[t][3], a0, a1, a2, a3, b0, b1);
+          }
+        }
+      }
+    }
+    // Lane (g, tq=0) holds columns 0,1 of rows g, g+8; lane (g, tq=1) column 2.
+#pragma unroll
+    for (int t = 0; t < MAXT; ++t) {
+      if (t < ntile) {
+        if (t == 0) {
+          d[0][0] += e[0]; d[0][1] += e[1]; d[0][2] += e[2]; d[0][3] += e[3];
+        }
+        float s0 = d[t][0] + d[t][1];
+        float s1 = d[t][2] + d[t][3];
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+        if (tq == 0) {
+          sm.partw[warp][t * 16 + g] = s0;
+          sm.partw[warp][t * 16 + g + 8] = s1;
+        }
       }
     }
     __syncwarp();
@@ -538,16 +629,73 @@ __device__ __noinline__ void gemv_mma(const KParams& P, Smem<S>& sm, const uint8
         mbar_arrive(&sm.empty[sl]);
       }
     }
-    kc += nch;
     consumer_sync(kConsumerThreads);
-    if (threadIdx.x < n) {
-      float tsum = 0.f;
+    if (threadIdx.x < ntile * 16) {
+      const int t = threadIdx.x >> 4, r = threadIdx.x & 15;
+      const int row = (t < t0n ? t * 16 : (t < t0n + t1n ? (t - t0n) * 16 : (t - t0n - t1n) * 16)) + r;
+      const int n = t < t0n ? n0 : (t < t0n + t1n ? n1 : n2);
+      float* out = t < t0n ? out0 : (t < t0n + t1n ? out1 : out2);
+      if (row < n) {
+        float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) tsum += sm.partw[w][threadIdx.x];
-      out[g0 - r0 + threadIdx.x] = tsum;
+        for (int w = 0; w < kConsumerWarps; w += 2) {
+          a0 += sm.partw[w][threadIdx.x];
+          a1 += sm.partw[w + 1][threadIdx.x];
+        }
+        float v = a0 + a1;
+        if (norm_scale) {
+          float ss = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w) ss += sm.red[w];
+          v *= rsqrtf(ss / (float)S::H + 1e-6f);
+        }
+        out[row] = v;
+      }
     }
     consumer_sync(kConsumerThreads);
+    return (uint32_t)nch;
   }
+};
+
+// Wait for n tagged fp32 words of an activation hop and stage them for the
+// next GEMV: optionally keep v in xres (residual stream), scale by the
+// RMSNorm gain (GAIN) and write the three bf16 split terms of the result to
+// xs.  Returns this thread's sum of v^2; callers that normalise reduce it
+// into sm.red (per warp) before the barrier that precedes GemvPlan::finish.
+template <class S, bool GAIN, bool RES, int kBatch>
+__device__ __forceinline__ float hop_to_xs(const KParams& P, Smem<S>& sm, const uint64_t* src, int n,
+                                           uint32_t tag, const GainRegs<S>& gr) {
+  float ss = 0.f;
+#pragma unroll 1
+  for (int base = threadIdx.x; base < n; base += kConsumerThreads * kBatch) {
+    uint64_t w[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = base + k * kConsumerThreads;
+      w[k] = i < n ? ld_relaxed(src + i) : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int i = base + k * kConsumerThreads;
+      if (i < n) {
+        if ((uint32_t)(w[k] >> 32) != tag) w[k] = poll_tagged_slow(P, sm, src + i, tag);
+        const float v = __uint_as_float((uint32_t)w[k]);
+        if (RES) sm.xres[i] = v;
+        ss = fmaf(v, v, ss);
+        float x = v;
+        if (GAIN) x = gr.g[k < GainRegs<S>::kPer ? k : 0] * v;
+        split_one(sm, i, x);
+      }
+    }
+  }
+  return ss;
+}
+
+// Per-warp partial of the RMSNorm sum of squares into sm.red[warp].
+template <class S>
+__device__ __forceinline__ void norm_partial(Smem<S>& sm, float ss) {
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = ss;
 }
 
 // LM head over rows [r0, r1) of the tied embedding: per-warp running argmax
@@ -555,9 +703,10 @@ __device__ __noinline__ void gemv_mma(const KParams& P, Smem<S>& sm, const uint8
 // lm_head_argmax_phase1 (src/sampling.cuh:32-89): a warp reads whole 2*H-byte
 // rows from shared memory instead of one thread walking each row.
 template <class S>
-__device__ __noinline__ void lm_rows(const KParams& P, Smem<S>& sm, const uint8_t* ring,
-                                        uint32_t& kc, int r0, int r1, float* logits_row0,
+__device__ MK_PHASE uint32_t lm_rows(const KParams& P, Smem<S>& sm, const uint8_t* ring,
+                                        uint32_t kc, int r0, int r1, float* logits_row0,
                                         float& best_v, int& best_i) {
+  const uint32_t kc0 = kc;
   constexpr int PPR = S::H / 256;
   constexpr int RB = 2 * S::H;
   constexpr int RPC = S::STB / RB;
@@ -591,40 +740,51 @@ __device__ __noinline__ void lm_rows(const KParams& P, Smem<S>& sm, const uint8_
     if (lane == 0) mbar_arrive(&sm.empty[slot]);
     ++kc;
   }
+  return kc - kc0;
 }
 
 }  // namespace mk
 
 namespace mk {
 
-// Online-softmax update over n positions whose K and V rows (D bf16 each) sit
-// contiguously in shared memory.  Scores: warp per position, lanes over D.
+// Online-softmax update over n1 + n2 positions whose K and V rows (D bf16
+// each) sit contiguously in shared memory: [0, n1) at K1/V1 (a ring stage),
+// [n1, n1 + n2) at K2/V2 (the previous and current positions).
+// Scores: one thread per (head, position), a full D-long dot product with no
+// cross-lane reduction; the 16-byte pieces of a row are visited in an order
+// rotated by the position so the rows a warp reads hit distinct banks.
 // PV: thread (part, g, d) sums positions = part (mod parts).  The running
 // (m, l) live in sm.mrun/lrun; the PV accumulator stays in `acc`.
 template <class S>
-__device__ __noinline__ void attend_block(Smem<S>& sm, const __nv_bfloat16* K,
-                                             const __nv_bfloat16* V, int n, float& acc) {
+__device__ MK_PHASE void attend_block(Smem<S>& sm, const __nv_bfloat16* K1, const __nv_bfloat16* V1,
+                                          int n1, const __nv_bfloat16* K2, const __nv_bfloat16* V2,
+                                          int n2, float& acc) {
   constexpr int D = S::D, GRP = S::GRP;
-  constexpr int EPL = D / 32;  // elements per lane
+  constexpr int PIECES = D / 8;  // 16-byte pieces per row
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = n1 + n2;
   const float scale = (D == 64) ? 0.125f : 0.08838834764831845f;  // D^-0.5
-  for (int pos = warp; pos < n; pos += kConsumerWarps) {
-    float kf[EPL];
-    if constexpr (EPL == 2) {
-      uint32_t w = *reinterpret_cast<const uint32_t*>(K + (size_t)pos * D + lane * 2);
-      kf[0] = bf_lo(w); kf[1] = bf_hi(w);
-    } else {
-      uint2 w = *reinterpret_cast<const uint2*>(K + (size_t)pos * D + lane * 4);
-      kf[0] = bf_lo(w.x); kf[1] = bf_hi(w.x); kf[2] = bf_lo(w.y); kf[3] = bf_hi(w.y);
-    }
+  for (int i = threadIdx.x; i < GRP * n; i += kConsumerThreads) {
+    const int g = i / n, pos = i - g * n;
+    const __nv_bfloat16* kr = pos < n1 ? K1 + (size_t)pos * D : K2 + (size_t)(pos - n1) * D;
+    const uint4* k4 = reinterpret_cast<const uint4*>(kr);
+    const float4* q4 = reinterpret_cast<const float4*>(&sm.qs[g][0]);
+    float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-    for (int g = 0; g < GRP; ++g) {
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) s = fmaf(sm.qs[g][lane * EPL + e], kf[e], s);
-      s = warp_sum(s);
-      if (lane == 0) sm.sc[g][pos] = s * scale;
+    for (int jj = 0; jj < PIECES; ++jj) {
+      const int j = (jj + pos) & (PIECES - 1);
+      const uint4 w = k4[j];
+      const float4 qa = q4[2 * j], qb = q4[2 * j + 1];
+      s0 = fmaf(bf_lo(w.x), qa.x, s0);
+      s1 = fmaf(bf_hi(w.x), qa.y, s1);
+      s0 = fmaf(bf_lo(w.y), qa.z, s0);
+      s1 = fmaf(bf_hi(w.y), qa.w, s1);
+      s0 = fmaf(bf_lo(w.z), qb.x, s0);
+      s1 = fmaf(bf_hi(w.z), qb.y, s1);
+      s0 = fmaf(bf_lo(w.w), qb.z, s0);
+      s1 = fmaf(bf_hi(w.w), qb.w, s1);
     }
+    sm.sc[g][pos] = (s0 + s1) * scale;
   }
   consumer_sync(kConsumerThreads);
   if (warp < GRP) {
@@ -637,7 +797,7 @@ __device__ __noinline__ void attend_block(Smem<S>& sm, const __nv_bfloat16* K,
     const float c = expf(mold - mnew);
     float sum = 0.f;
     for (int pos = lane; pos < n; pos += 32) {
-      float e = expf(sm.sc[g][pos] - mnew);
+      const float e = expf(sm.sc[g][pos] - mnew);
       sm.sc[g][pos] = e;
       sum += e;
     }
@@ -655,10 +815,17 @@ __device__ __noinline__ void attend_block(Smem<S>& sm, const __nv_bfloat16* K,
     constexpr int PARTS = kConsumerThreads / GD;
     const int tid = threadIdx.x;
     const int part = tid / GD, g = (tid / D) % GRP, d = tid % D;
-    float a = 0.f;
-    for (int pos = part; pos < n; pos += PARTS)
-      a = fmaf(sm.sc[g][pos], __bfloat162float(V[(size_t)pos * D + d]), a);
-    acc = acc * sm.corr[g] + a;
+    float a0 = 0.f, a1 = 0.f;
+    int pos = part;
+    for (; pos + PARTS < n1; pos += 2 * PARTS) {
+      a0 = fmaf(sm.sc[g][pos], __bfloat162float(V1[(size_t)pos * D + d]), a0);
+      a1 = fmaf(sm.sc[g][pos + PARTS], __bfloat162float(V1[(size_t)(pos + PARTS) * D + d]), a1);
+    }
+    for (; pos < n; pos += PARTS) {
+      const __nv_bfloat16 v = pos < n1 ? V1[(size_t)pos * D + d] : V2[(size_t)(pos - n1) * D + d];
+      a0 = fmaf(sm.sc[g][pos], __bfloat162float(v), a0);
+    }
+    acc = acc * sm.corr[g] + (a0 + a1);
   }
   consumer_sync(kConsumerThreads);
 }
@@ -669,8 +836,10 @@ __device__ __noinline__ void attend_block(Smem<S>& sm, const __nv_bfloat16* K,
 // (src/rmsnorm.cuh:57-84), apply_rope_inplace (src/attention.cuh:22-44),
 // append_kv (src/kv_cache.cuh:58-78) and warp_attention (src/attention.cuh:100-167).
 template <class S>
-__device__ __noinline__ void attention_item(const KParams& P, Smem<S>& sm, const uint8_t* ring, uint32_t& kc,
-                               int t, int l, int p, uint32_t seq, int h, int j, int nc, int item) {
+__device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const uint8_t* ring, uint32_t kc,
+                                           int t, int l, int p, uint32_t seq, int h, int j, int nc,
+                                           int item) {
+  const uint32_t kc0 = kc;
   constexpr int D = S::D, GRP = S::GRP, HALF = D / 2;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint64_t* qkv = P.hop + HopLayout<S>::QKV + (size_t)(l & 1) * S::QKV;
@@ -683,36 +852,44 @@ __device__ __noinline__ void attention_item(const KParams& P, Smem<S>& sm, const
   const int te = min(c1, p - 1);
 
   // Side inputs that do not depend on this step's activations are loaded into
-  // registers first, so their latency overlaps the wait for q, k, v:
-  // threads [0, D) gains, [D, D + D/2) RoPE row, [256, 256 + D) K/V of p-1.
-  float pre0 = 0.f, pre1 = 0.f;
+  // registers first, so their latency overlaps the wait for q, k, v: threads
+  // [0, D) load the q/k gains and the K/V of position p-1, threads [0, D/2)
+  // the RoPE row of position p.
+  static_assert(D <= kConsumerThreads, "one thread per head dimension");
+  float pre0 = 0.f, pre1 = 0.f, rc = 0.f, rs = 0.f;
   unsigned short prek = 0, prev_v = 0;
   if (tid < D) {
     pre0 = __bfloat162float(wptr(l, W_QNORM)[tid]);
     pre1 = __bfloat162float(wptr(l, W_KNORM)[tid]);
-  } else if (tid < D + HALF) {
-    pre0 = P.rope_cos[(size_t)p * HALF + (tid - D)];
-    pre1 = P.rope_sin[(size_t)p * HALF + (tid - D)];
-  } else if (prev && tid >= 256 && tid < 256 + D) {
-    // Written by the previous step (possibly another CTA): read through L2.
-    const unsigned short* kvu = reinterpret_cast<const unsigned short*>(P.kv);
-    prek = __ldcg(kvu + kv_index<S>(l, 0, h, p - 1, P.max_seq) + (tid - 256));
-    prev_v = __ldcg(kvu + kv_index<S>(l, 1, h, p - 1, P.max_seq) + (tid - 256));
+    if (tid < HALF) {
+      rc = P.rope_cos[(size_t)p * HALF + tid];
+      rs = P.rope_sin[(size_t)p * HALF + tid];
+    }
+    if (prev) {
+      // Written by the previous step (possibly another CTA): read through L2.
+      const unsigned short* kvu = reinterpret_cast<const unsigned short*>(P.kv);
+      prek = __ldcg(kvu + kv_index<S>(l, 0, h, p - 1, P.max_seq) + tid);
+      prev_v = __ldcg(kvu + kv_index<S>(l, 1, h, p - 1, P.max_seq) + tid);
+    }
   }
-  // Raw q (GRP heads), k, v of this KV head -> sm.pv as scratch [GRP+2][D].
-  float* raw = sm.pv;
+  // Raw q (GRP heads), k, v of this KV head -> sm.xin as scratch [GRP+2][D]
+  // (xin is free between the q/k/v GEMV and the merge).
+  static_assert((S::GRP + 2) * S::D <= S::XIN, "attention scratch");
+  float* raw = sm.xin;
   wait_tagged(P, sm, qkv + h * GRP * D, GRP * D, tq, raw);
   wait_tagged(P, sm, qkv + S::Q + h * D, D, tq, raw + GRP * D);
   wait_tagged(P, sm, qkv + S::Q + S::KV + h * D, D, tq, raw + (GRP + 1) * D);
   if (tid < D) {
     sm.gq[tid] = pre0;
     sm.gk[tid] = pre1;
-  } else if (tid < D + HALF) {
-    sm.rc[tid - D] = pre0;
-    sm.rs[tid - D] = pre1;
-  } else if (prev && tid >= 256 && tid < 256 + D) {
-    sm.kx[0][tid - 256] = __ushort_as_bfloat16(prek);
-    sm.vx[0][tid - 256] = __ushort_as_bfloat16(prev_v);
+    if (tid < HALF) {
+      sm.rc[tid] = rc;
+      sm.rs[tid] = rs;
+    }
+    if (prev) {
+      sm.kx[0][tid] = __ushort_as_bfloat16(prek);
+      sm.vx[0][tid] = __ushort_as_bfloat16(prev_v);
+    }
   }
   if (tid < GRP) { sm.mrun[tid] = -INFINITY; sm.lrun[tid] = 0.f; }
   consumer_sync(kConsumerThreads);
@@ -750,23 +927,14 @@ __device__ __noinline__ void attention_item(const KParams& P, Smem<S>& sm, const
     for (int d = lane; d < D; d += 32) sm.vx[1][d] = __float2bfloat16_rn(v[d]);
   }
   consumer_sync(kConsumerThreads);
-  if (last && tid < D) {
-    // Append the current K/V (bf16) at position p; later steps read it.
-    P.kv[kv_index<S>(l, 0, h, p, P.max_seq) + tid] = sm.kx[1][tid];
-    P.kv[kv_index<S>(l, 1, h, p, P.max_seq) + tid] = sm.vx[1][tid];
-    fence_proxy_async_global();
-    __threadfence();
-  }
   MK_DP(5);
 
   float acc = 0.f;
-  // Positions held outside the ring: p-1 (slot 0) and the current p (slot 1).
-  {
-    const int s0 = prev ? 0 : 1;
-    const int ne = (prev ? 1 : 0) + (last ? 1 : 0);
-    if (ne > 0) attend_block(sm, &sm.kx[s0][0], &sm.vx[s0][0], ne, acc);
-  }
-  MK_DP(6);
+  // Positions held outside the ring -- p-1 (slot 0) and the current p (slot
+  // 1) -- ride along with the first ring block (or form the only block).
+  const int s0 = prev ? 0 : 1;
+  int ne = (prev ? 1 : 0) + (last ? 1 : 0);
+  if (c0 >= te && ne > 0) attend_block(sm, &sm.kx[s0][0], &sm.vx[s0][0], ne, &sm.kx[0][0], &sm.vx[0][0], 0, acc);
   // Cached positions [c0, te) streamed through the ring as (K, V) stage pairs.
   for (int a = c0; a < te; a += S::SUBP) {
     const int n = min(S::SUBP, te - a);
@@ -776,8 +944,10 @@ __device__ __noinline__ void attention_item(const KParams& P, Smem<S>& sm, const
     const bool okv = okk && wait_bar(P, sm, &sm.full[sv], pv);
     if (!consumer_any(kConsumerThreads, !(okk && okv))) {
       attend_block(sm, reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sk * S::STB),
-                   reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sv * S::STB), n, acc);
+                   reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sv * S::STB), n,
+                   &sm.kx[s0][0], &sm.vx[s0][0], ne, acc);
     }
+    ne = 0;
     if (lane == 0) { mbar_arrive(&sm.empty[sk]); mbar_arrive(&sm.empty[sv]); }
     kc += 2;
   }
@@ -799,7 +969,18 @@ __device__ __noinline__ void attention_item(const KParams& P, Smem<S>& sm, const
     st_tagged(out + tid * (D + 2) + D, ta, __float_as_uint(sm.mrun[tid]));
     st_tagged(out + tid * (D + 2) + D + 1, ta, __float_as_uint(sm.lrun[tid]));
   }
+  if (last && tid < D) {
+    // Append the current K/V (bf16) at position p -- after the partial is
+    // published, so the fences stay off this step's critical path; the first
+    // reader of position p is the next step.
+    const int d = tid;
+    P.kv[kv_index<S>(l, 0, h, p, P.max_seq) + d] = sm.kx[1][d];
+    P.kv[kv_index<S>(l, 1, h, p, P.max_seq) + d] = sm.vx[1][d];
+    fence_proxy_async_global();
+    __threadfence();
+  }
   consumer_sync(kConsumerThreads);
+  return kc - kc0;
 }
 
 // Merge the split-KV partials of layer l into xin[Q] (every CTA, redundantly):
@@ -808,7 +989,7 @@ __device__ __noinline__ void attention_item(const KParams& P, Smem<S>& sm, const
 // of two chunks' {m, l, acc} at a time, so short contexts (nc <= 2) cost one
 // L2 round trip.  Also writes the bf16 split terms of each output.
 template <class S>
-__device__ __noinline__ void merge_attention(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc) {
+__device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc) {
   constexpr int D = S::D, GRP = S::GRP;
   constexpr int EPT = S::Q >= kConsumerThreads ? S::Q / kConsumerThreads : 1;
   static_assert(D % EPT == 0, "a thread's outputs stay inside one head");
@@ -884,30 +1065,50 @@ __device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint
     #pragma unroll 1
     for (int l = 0; l < S::L; ++l) {
       // ---- P1: x -> RMSNorm -> q, k, v rows --------------------------------
+      // RMSNorm is folded into the GEMV: W (g . x / rms) = (W (g . x)) / rms,
+      // so the GEMV runs on g . x while the sum of squares is reduced.
       GainRegs<S> gains;
       gains.load(wptr(l, W_ATTN_NORM));
-      if (l > 0)
-        wait_tagged(P, sm, P.hop + HopLayout<S>::X + (size_t)(l & 1) * S::H, S::H,
-                    tag_of(seq, l - 1, 4), sm.xres);
-      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
-      if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 1);
-      rmsnorm_to_xin(sm, gains);
-      MK_DP(1);
+      int s0, s1;
+      split_rows(S::QKV, N, cta, phase_rot(l, 0, N), s0, s1);
+      int rq[3], oq[3];
+#pragma unroll
+      for (int m = 0; m < 3; ++m) {
+        int a, b, o;
+        rq[m] = qkv_part<S>(s0, s1, m, a, b, o) ? b - a : 0;
+        oq[m] = rq[m] ? o - s0 : 0;
+      }
       {
-        int s0, s1;
-        split_rows(S::QKV, N, cta, phase_rot(l, 0, N), s0, s1);
-#pragma unroll 1
-        for (int m = 0; m < 3; ++m) {
-          int a, b, o;
-          if (qkv_part<S>(s0, s1, m, a, b, o))
-            gemv_mma<S, S::H>(P, sm, ring, kc, a, b, sm.rowsum[0] + (o - s0));
+        GemvPlan<S, S::H, 4> gp;
+        gp.prepare(P, sm, ring, kc, rq[0], rq[1], rq[2]);
+        float ss = 0.f;
+        if (l > 0) {
+          ss = hop_to_xs<S, true, true, GainRegs<S>::kPer>(P, sm, P.hop + HopLayout<S>::X + (size_t)(l & 1) * S::H, S::H,
+                                        tag_of(seq, l - 1, 4), gains);
+        } else {
+#pragma unroll
+          for (int e = 0; e < GainRegs<S>::kPer; ++e) {
+            const int i = tid + e * kConsumerThreads;
+            if (i < S::H) {
+              const float v = sm.xres[i];
+              ss = fmaf(v, v, ss);
+              split_one(sm, i, gains.g[e] * v);
+            }
+          }
         }
-        MK_DP(2);
+        norm_partial(sm, ss);
+        if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 1);
+        MK_DP(1);
+        kc += gp.finish(P, sm, sm.rowsum[0] + oq[0], sm.rowsum[0] + oq[1], sm.rowsum[0] + oq[2], true);
+      }
+      MK_DP(2);
+      {
         uint64_t* dst = P.hop + HopLayout<S>::QKV + (size_t)(l & 1) * S::QKV;
         const uint32_t tg = tag_of(seq, l, 0);
         for (int r = tid; r < s1 - s0; r += kConsumerThreads)
           st_tagged(dst + s0 + r, tg, __float_as_uint(sm.rowsum[0][r]));
-        consumer_sync(kConsumerThreads);
+        // (no barrier needed: the next writer of rowsum[0] is behind several)
         if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 2);
       }
       // ---- P2: attention items owned by this CTA ------------------------------
@@ -915,39 +1116,42 @@ __device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint
         int ilo, ihi;
         items_of_cta(cta, l, nitems, N, ilo, ihi);
         for (int i = ilo; i < ihi; ++i)
-          attention_item<S>(P, sm, ring, kc, t, l, p, seq, i / nc, i % nc, nc, i);
+          kc += attention_item<S>(P, sm, ring, kc, t, l, p, seq, i / nc, i % nc, nc, i);
       }
       // ---- P3: merge -> O projection + residual --------------------------------
-      MK_DP(8);
-      merge_attention<S>(P, sm, l, seq, nc);
-      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
-      if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 3);
       {
         int r0, r1;
         split_rows(S::H, N, cta, phase_rot(l, 1, N), r0, r1);
-        gemv_mma<S, S::Q>(P, sm, ring, kc, r0, r1, sm.rowsum[0]);
+        GemvPlan<S, S::Q, 2> gp;
+        gp.prepare(P, sm, ring, kc, r1 - r0, 0, 0);
+        MK_DP(8);
+        merge_attention<S>(P, sm, l, seq, nc);
+        if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 3);
+        kc += gp.finish(P, sm, sm.rowsum[0], nullptr, nullptr, false);
         MK_DP(10);
         uint64_t* dst = P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H;
         const uint32_t tg = tag_of(seq, l, 2);
         for (int r = tid; r < r1 - r0; r += kConsumerThreads)
           st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
-        consumer_sync(kConsumerThreads);
         if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 4);
       }
       // ---- P4: x' -> RMSNorm -> silu(gate) * up ---------------------------------
-      gains.load(wptr(l, W_FFN_NORM));
-      wait_tagged(P, sm, P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H, S::H,
-                  tag_of(seq, l, 2), sm.xres);
-      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
-      MK_DP(12);
-      rmsnorm_to_xin(sm, gains);
-      MK_DP(13);
       {
+        gains.load(wptr(l, W_FFN_NORM));
         int r0, r1;
         split_rows(S::I, N, cta, phase_rot(l, 2, N), r0, r1);
-        gemv_mma<S, S::H>(P, sm, ring, kc, r0, r1, sm.rowsum[0]);
-        MK_DP(14);
-        gemv_mma<S, S::H>(P, sm, ring, kc, r0, r1, sm.rowsum[1]);
+        GemvPlan<S, S::H, 4> gp;
+        gp.prepare(P, sm, ring, kc, r1 - r0, r1 - r0, 0);
+        // xres is rewritten by the hop below: every thread must be done with
+        // the O epilogue's reads of it.
+        consumer_sync(kConsumerThreads);
+        const float ss = hop_to_xs<S, true, true, GainRegs<S>::kPer>(P, sm, P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H,
+                                                  S::H, tag_of(seq, l, 2), gains);
+        norm_partial(sm, ss);
+        if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+        MK_DP(13);
+        kc += gp.finish(P, sm, sm.rowsum[0], sm.rowsum[1], nullptr, true);
         MK_DP(15);
         uint64_t* dst = P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I;
         const uint32_t tg = tag_of(seq, l, 3);
@@ -957,19 +1161,19 @@ __device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint
           const float hval = (g / (1.0f + expf(-g))) * u;
           st_tagged(dst + r0 + r, tg, __float_as_uint(hval));
         }
-        consumer_sync(kConsumerThreads);
         if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 5);
       }
       // ---- P5: h -> down projection + residual --------------------------------
-      wait_tagged(P, sm, P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I, S::I,
-                  tag_of(seq, l, 3), sm.xin);
-      if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
-      split_xin(sm, S::I);
-      MK_DP(17);
       {
         int r0, r1;
         split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
-        gemv_mma<S, S::I>(P, sm, ring, kc, r0, r1, sm.rowsum[0]);
+        GemvPlan<S, S::I, 2> gp;
+        gp.prepare(P, sm, ring, kc, r1 - r0, 0, 0);
+        hop_to_xs<S, false, false, (S::I + kConsumerThreads - 1) / kConsumerThreads>(P, sm, P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I, S::I,
+                                   tag_of(seq, l, 3), gains);
+        if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+        MK_DP(17);
+        kc += gp.finish(P, sm, sm.rowsum[0], nullptr, nullptr, false);
         MK_DP(18);
         uint64_t* dst = P.hop + HopLayout<S>::X + (size_t)((l + 1) & 1) * S::H;
         const uint32_t tg = tag_of(seq, l, 4);
@@ -977,6 +1181,7 @@ __device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint
         if (!skip)
           for (int r = tid; r < r1 - r0; r += kConsumerThreads)
             st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
+        // xres is rewritten by the next layer's hop: finish the reads first.
         consumer_sync(kConsumerThreads);
         if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 6);
       }
@@ -995,7 +1200,7 @@ __device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint
       float bv = -INFINITY;
       int bi = 0x7fffffff;
       float* lrow = P.logits ? P.logits + (size_t)t * S::V : nullptr;
-      lm_rows<S>(P, sm, ring, kc, r0, r1, lrow, bv, bi);
+      kc += lm_rows<S>(P, sm, ring, kc, r0, r1, lrow, bv, bi);
       if (lane == 0) { sm.red[warp] = bv; sm.redi[warp] = bi; }
       consumer_sync(kConsumerThreads);
       uint64_t* lm = P.hop + HopLayout<S>::LM + (size_t)(t & 1) * kMaxCtas * 2;

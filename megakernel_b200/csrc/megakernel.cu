@@ -105,6 +105,24 @@ bool rows_fit(const ShapeInfo& s, int N) {
          rows(s.I) <= mk::kRowsMax && N <= mk::kMaxCtas;
 }
 
+// The tensor-core GEMV takes a phase's segments in one pass: every segment
+// <= 32 rows, <= 4 tiles of 16 rows per pass, and all stages of the pass in
+// the ring at once.
+template <class S>
+bool plan_fits(int N, int nst) {
+  auto rows = [&](int R) { return (R + N - 1) / N; };
+  auto chunks = [](int r, int rpc) { return (r + rpc - 1) / rpc; };
+  const int rq = rows(S::QKV), rh = rows(S::H), ri = rows(S::I);
+  const int rpc_h = S::template rows_per_stage<S::H>();
+  if (rq > 32 || rh > 32 || ri > 32) return false;
+  if ((rq + 15) / 16 + 2 > 4) return false;                        // q/k/v tiles
+  if (chunks(rq, rpc_h) + 2 > nst) return false;
+  if (2 * chunks(ri, rpc_h) > nst) return false;                   // gate + up
+  if (chunks(rh, S::template rows_per_stage<S::Q>()) > nst) return false;
+  if (chunks(rh, S::template rows_per_stage<S::I>()) > nst) return false;
+  return N <= mk::kMaxCtas;
+}
+
 template <class S>
 void kernel_info(State* st) {
   st->kernel = reinterpret_cast<const void*>(&mk::decode_kernel<S>);
@@ -199,7 +217,13 @@ int init_impl(void* d_weights, const long long* offsets, int num_offsets, const 
           cudaSuccess || occ < 1)
     return bail(MK_ERR_LAUNCH);
   st->ncta = o->num_ctas > 0 ? o->num_ctas : sms;
-  if (st->ncta > sms * occ || !rows_fit(s, st->ncta)) return bail(MK_ERR_INVALID_ARG);
+  bool fits = false;
+  switch (id) {
+    case 0: fits = plan_fits<mk::ShapeD64>(st->ncta, st->nst); break;
+    case 1: fits = plan_fits<mk::ShapeD128>(st->ncta, st->nst); break;
+    default: fits = plan_fits<mk::ShapeTiny>(st->ncta, st->nst); break;
+  }
+  if (st->ncta > sms * occ || !rows_fit(s, st->ncta) || !fits) return bail(MK_ERR_INVALID_ARG);
 
   if (cudaStreamCreateWithFlags(&st->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(MK_ERR_CUDA);

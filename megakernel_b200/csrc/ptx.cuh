@@ -111,14 +111,18 @@ __device__ __forceinline__ bool consumer_any(int nthreads, bool pred) {
 // ---- warp-level tensor-core GEMV pieces -----------------------------------
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& a0, uint32_t& a1, uint32_t& a2,
                                             uint32_t& a3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(addr));
+  // Not volatile: callers only read stages whose full barrier they already
+  // waited on (the wait is an asm volatile with a memory clobber, which this
+  // "memory"-clobbering load stays behind), so the compiler may schedule the
+  // loads of an unrolled loop ahead of the MMAs.
+  asm("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+      : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3) : "r"(addr) : "memory");
 }
 // D[16x8] += A[16x16] (bf16, row) * B[16x8] (bf16, col), fp32 accumulate.
 __device__ __forceinline__ void mma_bf16_16816(float& d0, float& d1, float& d2, float& d3, uint32_t a0,
                                                uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                                uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
       "{%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)

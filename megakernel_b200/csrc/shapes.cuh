@@ -9,7 +9,7 @@
 
 namespace mk {
 
-constexpr int kConsumerWarps = 16;
+constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;  // + one producer warp
 constexpr int kRingBytes = 176 * 1024;
