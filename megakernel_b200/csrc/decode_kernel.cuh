@@ -67,6 +67,7 @@ struct KParams {
   int max_seq;
   int ncta;
   int nst;                        // ring stages in use (<= S::NST)
+  int issue_gap_ns;               // producer pacing: min ns between stage issues (0 = off)
   long long timeout_ns;
   int debug_skip_cta;             // >= 0: that CTA never publishes layer-0 x (fault test)
   uint64_t* trace;                // optional stamps [trace_steps][ncta][Trace::kPoints]
@@ -136,6 +137,7 @@ struct Smem {
   alignas(16) __nv_bfloat16 kx[2][S::D];
   alignas(16) __nv_bfloat16 vx[2][S::D];
   float red[kConsumerWarps * 2];
+  float mlbuf[S::NQ * kMaxChunksPerHead * 2];  // attention partials' (m, l), one copy per CTA
   int redi[kConsumerWarps];
   int next_token;
   volatile int abort_flag;
@@ -199,6 +201,7 @@ __device__ __noinline__ uint64_t poll_tagged_slow(const KParams& P, Smem<S>& sm,
   do {
     v = ld_relaxed(src);
     if ((uint32_t)(v >> 32) == tag) break;
+    __nanosleep(200);
   } while (sp.keep_going(P, sm));
   return v;
 }
@@ -247,11 +250,20 @@ struct Producer {
   uint32_t nst;
   uint32_t k;       // stages issued so far
   bool ok;
+  uint64_t last;    // globaltimer of the last issue (pacing)
 
   __device__ __noinline__ bool acquire(uint32_t& slot) {
     slot = k % nst;
     const uint32_t ph = (k / nst) & 1u;
     if (!wait_bar(*P, *sm, &sm->empty[slot], ph ^ 1u)) ok = false;
+    // Pacing: spread ring refills out instead of re-issuing every freed stage
+    // at once, so weight reads do not flood the memory system in bursts
+    // exactly when activations are being exchanged.
+    if (ok && P->issue_gap_ns > 0) {
+      uint64_t now = globaltimer_ns();
+      while (now - last < (uint64_t)P->issue_gap_ns) now = globaltimer_ns();
+      last = now;
+    }
     return ok;
   }
   // Contiguous bytes (LM-head rows, cached K/V): one copy per stage.
@@ -332,6 +344,7 @@ __device__ __noinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ri
   Producer<S>& pr = *reinterpret_cast<Producer<S>*>(sm.prod);
   pr.k = 0;
   pr.ok = true;
+  pr.last = 0;
   pr.P = &P;
   pr.sm = &sm;
   pr.ring = ring;
@@ -374,6 +387,33 @@ __device__ __noinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ri
 
 namespace mk {
 
+// Resolve up to NB tagged words already loaded into w[]: while any of them
+// lacks `tag`, re-load ALL of the missing ones together, so a round of
+// polling costs one L2 round trip however many words a thread owns.
+// Bounded like every wait; on expiry the caller proceeds with stale values
+// (the abort flag is set and the step is abandoned at the next barrier).
+template <class S, int NB>
+__device__ __forceinline__ void resolve_tagged(const KParams& P, Smem<S>& sm, uint64_t (&w)[NB],
+                                               const uint64_t* (&src)[NB], int nvalid, uint32_t tag) {
+  bool miss = false;
+#pragma unroll
+  for (int k = 0; k < NB; ++k) miss |= (k < nvalid) && (uint32_t)(w[k] >> 32) != tag;
+  if (!miss) return;
+  Spin sp;
+  while (miss && sp.keep_going(P, sm)) {
+    // Back off between rounds: every CTA polls the same words, and re-issuing
+    // all of them back to back floods the L2 slices that hold them (the
+    // writers' stores queue behind the polls).
+    __nanosleep(200);
+#pragma unroll
+    for (int k = 0; k < NB; ++k)
+      if (k < nvalid && (uint32_t)(w[k] >> 32) != tag) w[k] = ld_relaxed(src[k]);
+    miss = false;
+#pragma unroll
+    for (int k = 0; k < NB; ++k) miss |= (k < nvalid) && (uint32_t)(w[k] >> 32) != tag;
+  }
+}
+
 // ---- consumer helpers (all 512 consumer threads call these) -----------------
 
 // Spin on n tagged words src[i] until each carries `tag`; store the fp32
@@ -392,12 +432,18 @@ __device__ MK_PHASE void wait_tagged(const KParams& P, Smem<S>& sm, const uint64
       const int i = base + k * kConsumerThreads;
       v[k] = i < n ? ld_relaxed(src + i) : 0;
     }
+    const uint64_t* sp[kBatch];
+    int nv = 0;
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      sp[k] = src + base + k * kConsumerThreads;
+      nv += (base + k * kConsumerThreads < n) ? 1 : 0;
+    }
+    resolve_tagged<S, kBatch>(P, sm, v, sp, nv, tag);
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
       const int i = base + k * kConsumerThreads;
-      if (i >= n) break;
-      if ((uint32_t)(v[k] >> 32) != tag) v[k] = poll_tagged_slow(P, sm, src + i, tag);
-      dst[i] = __uint_as_float((uint32_t)v[k]);
+      if (i < n) dst[i] = __uint_as_float((uint32_t)v[k]);
     }
   }
   if (tw0 != 0) sm.wait_hop_ns += globaltimer_ns() - tw0;
@@ -674,11 +720,18 @@ __device__ __forceinline__ float hop_to_xs(const KParams& P, Smem<S>& sm, const 
       const int i = base + k * kConsumerThreads;
       w[k] = i < n ? ld_relaxed(src + i) : 0;
     }
+    const uint64_t* sp[kBatch];
+    int nv = 0;
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      sp[k] = src + base + k * kConsumerThreads;
+      nv += (base + k * kConsumerThreads < n) ? 1 : 0;
+    }
+    resolve_tagged<S, kBatch>(P, sm, w, sp, nv, tag);
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
       const int i = base + k * kConsumerThreads;
       if (i < n) {
-        if ((uint32_t)(w[k] >> 32) != tag) w[k] = poll_tagged_slow(P, sm, src + i, tag);
         const float v = __uint_as_float((uint32_t)w[k]);
         if (RES) sm.xres[i] = v;
         ss = fmaf(v, v, ss);
@@ -876,9 +929,23 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
   // (xin is free between the q/k/v GEMV and the merge).
   static_assert((S::GRP + 2) * S::D <= S::XIN, "attention scratch");
   float* raw = sm.xin;
-  wait_tagged(P, sm, qkv + h * GRP * D, GRP * D, tq, raw);
-  wait_tagged(P, sm, qkv + S::Q + h * D, D, tq, raw + GRP * D);
-  wait_tagged(P, sm, qkv + S::Q + S::KV + h * D, D, tq, raw + (GRP + 1) * D);
+  {
+    // q (GRP heads), k and v of head h: up to three words per thread,
+    // resolved together (one L2 round trip per polling round).
+    static_assert(GRP * D <= kConsumerThreads, "one q word per thread");
+    const uint64_t* sp[3] = {qkv + h * GRP * D + tid, qkv + S::Q + h * D + tid,
+                             qkv + S::Q + S::KV + h * D + tid};
+    const int nv = tid < D ? 3 : (tid < GRP * D ? 1 : 0);
+    uint64_t w[3] = {0, 0, 0};
+    if (nv > 0) w[0] = ld_relaxed(sp[0]);
+    if (nv > 1) { w[1] = ld_relaxed(sp[1]); w[2] = ld_relaxed(sp[2]); }
+    resolve_tagged<S, 3>(P, sm, w, sp, nv, tq);
+    if (nv > 0) raw[tid] = __uint_as_float((uint32_t)w[0]);
+    if (nv > 1) {
+      raw[GRP * D + tid] = __uint_as_float((uint32_t)w[1]);
+      raw[(GRP + 1) * D + tid] = __uint_as_float((uint32_t)w[2]);
+    }
+  }
   if (tid < D) {
     sm.gq[tid] = pre0;
     sm.gk[tid] = pre1;
@@ -969,6 +1036,7 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
     st_tagged(out + tid * (D + 2) + D, ta, __float_as_uint(sm.mrun[tid]));
     st_tagged(out + tid * (D + 2) + D + 1, ta, __float_as_uint(sm.lrun[tid]));
   }
+  MK_DP(6);
   if (last && tid < D) {
     // Append the current K/V (bf16) at position p -- after the partial is
     // published, so the fences stay off this step's critical path; the first
@@ -984,10 +1052,11 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
 }
 
 // Merge the split-KV partials of layer l into xin[Q] (every CTA, redundantly):
-// out = sum_j exp(m_j - M) acc_j / sum_j exp(m_j - M) l_j, as an online merge.
-// Thread t owns EPT consecutive outputs of one query head; it issues the loads
-// of two chunks' {m, l, acc} at a time, so short contexts (nc <= 2) cost one
-// L2 round trip.  Also writes the bf16 split terms of each output.
+// out = sum_j exp(m_j - M) acc_j / sum_j exp(m_j - M) l_j.
+// Each CTA polls every partial word exactly once per round: the per-head
+// (m, l) pairs by a few threads into shared memory, then each thread its EPT
+// accumulator words of every chunk (resolved together, one L2 round trip per
+// polling round).  Also writes the bf16 split terms of each output.
 template <class S>
 __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc) {
   constexpr int D = S::D, GRP = S::GRP;
@@ -995,55 +1064,56 @@ __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, u
   static_assert(D % EPT == 0, "a thread's outputs stay inside one head");
   const uint64_t* att = P.hop + HopLayout<S>::ATT + (size_t)(l & 1) * HopLayout<S>::kAttWords;
   const uint32_t ta = tag_of(seq, l, 1);
-  const int e0 = threadIdx.x * EPT;
-  if (e0 >= S::Q) return;
-  const int qh = e0 / D, d0 = e0 % D, g = qh % GRP;
   const size_t stride = (size_t)GRP * (D + 2);
-  const uint64_t* b = att + ((size_t)(qh / GRP) * nc * GRP + g) * (D + 2);
-  float M = -INFINITY, den = 0.f, acc[EPT];
-#pragma unroll
-  for (int k = 0; k < EPT; ++k) acc[k] = 0.f;
-  for (int j0 = 0; j0 < nc; j0 += 2) {
-    uint64_t w[2][EPT + 2];
-#pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      if (j0 + jj >= nc) break;
-      const uint64_t* bj = b + (size_t)(j0 + jj) * stride;
-      w[jj][0] = ld_relaxed(bj + D);
-      w[jj][1] = ld_relaxed(bj + D + 1);
-#pragma unroll
-      for (int k = 0; k < EPT; ++k) w[jj][2 + k] = ld_relaxed(bj + d0 + k);
-    }
-#pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      if (j0 + jj >= nc) break;
-      const uint64_t* bj = b + (size_t)(j0 + jj) * stride;
-      float f[EPT + 2];
-#pragma unroll
-      for (int k = 0; k < EPT + 2; ++k) {
-        const uint64_t* src = bj + (k == 0 ? D : k == 1 ? D + 1 : d0 + k - 2);
-        f[k] = (uint32_t)(w[jj][k] >> 32) == ta ? __uint_as_float((uint32_t)w[jj][k])
-                                                : wait_word(P, sm, src, ta);
-      }
-      const float mn = fmaxf(M, f[0]);
-      const float c = expf(M - mn), cj = expf(f[0] - mn);
-      den = den * c + f[1] * cj;
-#pragma unroll
-      for (int k = 0; k < EPT; ++k) acc[k] = acc[k] * c + f[2 + k] * cj;
-      M = mn;
-    }
+  // (m, l) of every (query head, chunk): word pairs at item * stride + g * (D+2) + D.
+  for (int i = threadIdx.x; i < S::NQ * nc; i += kConsumerThreads) {
+    const int qh = i / nc, j = i % nc;
+    const uint64_t* bj = att + ((size_t)(qh / GRP) * nc + j) * stride + (size_t)(qh % GRP) * (D + 2) + D;
+    uint64_t w2[2] = {ld_relaxed(bj), ld_relaxed(bj + 1)};
+    const uint64_t* sp2[2] = {bj, bj + 1};
+    resolve_tagged<S, 2>(P, sm, w2, sp2, 2, ta);
+    sm.mlbuf[2 * i] = __uint_as_float((uint32_t)w2[0]);
+    sm.mlbuf[2 * i + 1] = __uint_as_float((uint32_t)w2[1]);
   }
-  const float inv = 1.f / den;
+  const int e0 = threadIdx.x * EPT;
+  const bool active = e0 < S::Q;
+  const int qh = active ? e0 / D : 0, d0 = e0 % D, g = qh % GRP;
+  const uint64_t* b = att + ((size_t)(qh / GRP) * nc * GRP + g) * (D + 2);
+  // Accumulator words: all chunks' EPT words loaded up front (nc <= 8).
+  uint64_t w[kMaxChunksPerHead * EPT];
+  const uint64_t* sp[kMaxChunksPerHead * EPT];
 #pragma unroll
-  for (int k = 0; k < EPT; ++k) {
-    sm.xin[e0 + k] = acc[k] * inv;
-    split_one(sm, e0 + k, acc[k] * inv);
+  for (int j = 0; j < kMaxChunksPerHead; ++j)
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      sp[j * EPT + k] = b + (size_t)j * stride + d0 + k;
+      w[j * EPT + k] = (active && j < nc) ? ld_relaxed(sp[j * EPT + k]) : 0;
+    }
+  if (active) resolve_tagged<S, kMaxChunksPerHead * EPT>(P, sm, w, sp, nc * EPT, ta);
+  consumer_sync(kConsumerThreads);
+  if (active) {
+    float M = -INFINITY;
+    for (int j = 0; j < nc; ++j) M = fmaxf(M, sm.mlbuf[2 * (qh * nc + j)]);
+    float den = 0.f, acc[EPT];
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) acc[k] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxChunksPerHead; ++j) {
+      if (j < nc) {
+        const float cj = expf(sm.mlbuf[2 * (qh * nc + j)] - M);
+        den = fmaf(sm.mlbuf[2 * (qh * nc + j) + 1], cj, den);
+#pragma unroll
+        for (int k = 0; k < EPT; ++k) acc[k] = fmaf(__uint_as_float((uint32_t)w[j * EPT + k]), cj, acc[k]);
+      }
+    }
+    const float inv = 1.f / den;
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      sm.xin[e0 + k] = acc[k] * inv;
+      split_one(sm, e0 + k, acc[k] * inv);
+    }
   }
 }
-
-}  // namespace mk
-
-namespace mk {
 
 template <class S>
 __device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, int cta) {
@@ -1127,6 +1197,7 @@ __device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint
         MK_DP(8);
         merge_attention<S>(P, sm, l, seq, nc);
         if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
+        MK_DP(9);
         if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 3);
         kc += gp.finish(P, sm, sm.rowsum[0], nullptr, nullptr, false);
         MK_DP(10);
@@ -1217,8 +1288,11 @@ __device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint
       // Every CTA reduces all CTAs' (max, index) pairs: lowest index wins ties.
       float* pairs = &sm.partw[0][0];
       for (int c = tid; c < N; c += kConsumerThreads) {
-        pairs[c] = wait_word(P, sm, lm + 2 * c, tg);
-        pairs[kMaxCtas + c] = wait_word(P, sm, lm + 2 * c + 1, tg);
+        uint64_t w2[2] = {ld_relaxed(lm + 2 * c), ld_relaxed(lm + 2 * c + 1)};
+        const uint64_t* sp2[2] = {lm + 2 * c, lm + 2 * c + 1};
+        resolve_tagged<S, 2>(P, sm, w2, sp2, 2, tg);
+        pairs[c] = __uint_as_float((uint32_t)w2[0]);
+        pairs[kMaxCtas + c] = __uint_as_float((uint32_t)w2[1]);
       }
       consumer_sync(kConsumerThreads);
       if (warp == 0) {

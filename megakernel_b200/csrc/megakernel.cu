@@ -27,6 +27,7 @@ struct State {
   int device = 0;
   int ncta = 0;
   int nst = 0;                  // ring stages in use
+  int issue_gap_ns = 0;         // producer pacing (MK_ISSUE_GAP_NS tuning knob)
   int max_seq = 0;
   int pos = 0;
   uint32_t seq = 1;
@@ -134,6 +135,7 @@ void kernel_info(State* st) {
     const int v = std::atoi(e);
     if (v >= 4 && v < S::NST) st->nst = v;
   }
+  if (const char* e = std::getenv("MK_ISSUE_GAP_NS")) st->issue_gap_ns = std::atoi(e);
 }
 
 void free_state(State* st) {
@@ -291,6 +293,7 @@ int launch(State* st, const int* d_forced, int n_forced, int n_steps, int* d_out
   P.max_seq = st->max_seq;
   P.ncta = st->ncta;
   P.nst = st->nst;
+  P.issue_gap_ns = st->issue_gap_ns;
   P.timeout_ns = st->timeout_ns;
   P.debug_skip_cta = st->debug_skip_cta;
   P.trace = st->d_trace;

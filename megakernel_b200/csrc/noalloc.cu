@@ -146,6 +146,7 @@ extern "C" int megakernel_decode_noalloc(const void* d_weights, const long long*
   P.max_seq = kv_max_seq;
   P.ncta = s->sms;
   P.nst = SNA::NST;
+  P.issue_gap_ns = 0;
   P.timeout_ns = 1000000000LL;
   P.debug_skip_cta = -1;
   P.trace = nullptr;
