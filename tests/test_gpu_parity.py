@@ -213,3 +213,35 @@ def test_timeout_reports_error_and_handle_recovers():
     g = golden("tiny")
     toks, lg = teacher_forced(engine("tiny"), g["seq"].tolist()[:4])
     assert np.abs(lg[:, g["sub_ids"]] - g["sub_logits"][:4]).max() < LOGIT_TOL
+
+
+def test_long_context_prefilled_kv_vs_oracle():
+    """K/V of positions 0..8191 in every layer set to
+    bf16(N(0,1)) (seed 2), then decode from position 8192 (split-KV across
+    CTAs).  Compared with the fp32 oracle given the same cache."""
+    shape, w, flat, offs = weights("qwen3-0.6b-d64")
+    P0, steps = 8192, 4
+    eng = MegakernelEngine(flat=flat, offsets=offs, shape=shape, max_seq=P0 + 64,
+                           timeout_ns=2_000_000_000)
+    g = torch.Generator().manual_seed(2)
+    kv_host = torch.randn(shape.layers, 2, shape.kv_heads, P0, shape.head_dim, generator=g)
+    kv_host = kv_host.to(torch.bfloat16)
+    kv = eng.kv_cache()
+    kv[:, :, :, :P0] = kv_host.to(DEV)
+    torch.cuda.synchronize()
+    eng.set_pos(P0)
+    seq = golden("qwen3-0.6b-d64")["seq"][:steps].tolist()
+    toks = torch.tensor(seq, dtype=torch.int32, device=DEV)
+    out = torch.zeros(steps, dtype=torch.int32, device=DEV)
+    lg = torch.zeros(steps, shape.vocab, device=DEV)
+    eng.decode_n(toks, steps, out, logits=lg)
+    o = Qwen3DecodeOracle(shape, w, kv_bf16=True, max_seq=P0 + 8, device="cuda")
+    for layer in range(shape.layers):
+        o.set_kv(layer, kv_host[layer, 0], kv_host[layer, 1])
+    o.pos = P0
+    otoks, olg, omargin = o.run(seq, steps)
+    err = np.abs(lg.cpu().numpy() - olg).max()
+    assert err < LOGIT_TOL, err
+    ok = omargin > MARGIN
+    assert np.array_equal(out.cpu().numpy()[ok], otoks[ok])
+    eng.close()
