@@ -28,14 +28,10 @@
 #include "ptx.cuh"
 #include "shapes.cuh"
 
-// Phase functions are inlined into the consumer loop (measured faster than
-// out-of-line calls, whose register save/restore goes through local memory);
-// MK_INLINE_PHASES=0 keeps them out of line for code-size experiments.
-#if defined(MK_INLINE_PHASES) && !MK_INLINE_PHASES
-#define MK_PHASE __noinline__
-#else
+// Everything is inlined into the kernel body: the consumer and producer
+// warpgroups run with different register budgets (setmaxnreg), and ptxas
+// drops setmaxnreg when the kernel makes out-of-line calls.
 #define MK_PHASE __forceinline__
-#endif
 
 namespace mk {
 
@@ -180,7 +176,7 @@ struct Spin {
 // stays a couple of instructions at every call site, which keeps the kernel's
 // hot loop small enough for the instruction caches.
 template <class S>
-__device__ __noinline__ bool wait_bar_slow(const KParams& P, Smem<S>& sm, uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool wait_bar_slow(const KParams& P, Smem<S>& sm, uint64_t* bar, uint32_t parity) {
   Spin sp;
   while (!mbar_try_wait(bar, parity)) {
     if (!sp.keep_going(P, sm)) return false;
@@ -194,7 +190,7 @@ __device__ __forceinline__ bool wait_bar(const KParams& P, Smem<S>& sm, uint64_t
 }
 // Re-poll one tagged word until it carries `tag` (bounded); returns the word.
 template <class S>
-__device__ __noinline__ uint64_t poll_tagged_slow(const KParams& P, Smem<S>& sm, const uint64_t* src,
+__device__ __forceinline__ uint64_t poll_tagged_slow(const KParams& P, Smem<S>& sm, const uint64_t* src,
                                                   uint32_t tag) {
   uint64_t v;
   Spin sp;
@@ -252,7 +248,7 @@ struct Producer {
   bool ok;
   uint64_t last;    // globaltimer of the last issue (pacing)
 
-  __device__ __noinline__ bool acquire(uint32_t& slot) {
+  __device__ __forceinline__ bool acquire(uint32_t& slot) {
     slot = k % nst;
     const uint32_t ph = (k / nst) & 1u;
     if (!wait_bar(*P, *sm, &sm->empty[slot], ph ^ 1u)) ok = false;
@@ -267,14 +263,14 @@ struct Producer {
     return ok;
   }
   // Contiguous bytes (LM-head rows, cached K/V): one copy per stage.
-  __device__ __noinline__ void issue(const void* src, uint32_t bytes) {
+  __device__ __forceinline__ void issue(const void* src, uint32_t bytes) {
     uint32_t slot;
     if (!ok || !acquire(slot)) return;
     mbar_arrive_expect_tx(&sm->full[slot], bytes);
     bulk_g2s(ring + (size_t)slot * S::STB, src, bytes, &sm->full[slot], pol);
     ++k;
   }
-  __device__ __noinline__ void rows(const __nv_bfloat16* base, int r0, int r1, int K) {
+  __device__ __forceinline__ void rows(const __nv_bfloat16* base, int r0, int r1, int K) {
     const int rpc = S::STB / (2 * K);
     for (int r = r0; r < r1 && ok; r += rpc) {
       const int n = min(rpc, r1 - r);
@@ -282,7 +278,7 @@ struct Producer {
     }
   }
   // Rows for the tensor-core GEMV: one copy per row, at pitch 2K + 16.
-  __device__ __noinline__ void rows_padded(const __nv_bfloat16* base, int r0, int r1, int K) {
+  __device__ __forceinline__ void rows_padded(const __nv_bfloat16* base, int r0, int r1, int K) {
     const int pitch = 2 * K + kRowPad;
     const int rpc = S::STB / pitch;
     for (int r = r0; r < r1 && ok; r += rpc) {
@@ -300,7 +296,7 @@ struct Producer {
   // < p-1 were written by steps <= t-2 of this launch (or earlier launches):
   // wait until the consumers have finished step t-2 before reading them.
   // Position p-1 is read by the consumers directly (written by step t-1).
-  __device__ __noinline__ void kv_items(int t, int l, int p, int nc, int ilo, int ihi) {
+  __device__ __forceinline__ void kv_items(int t, int l, int p, int nc, int ilo, int ihi) {
     for (int i = ilo; i < ihi && ok; ++i) {
       const int h = i / nc, j = i % nc;
       int c0, c1;
@@ -323,7 +319,7 @@ struct Producer {
   }
   // Abandoned: wait (bounded) for the copies already in flight so that no
   // bulk copy lands in shared memory after this CTA has exited.
-  __device__ __noinline__ void drain() {
+  __device__ __forceinline__ void drain() {
     const uint32_t first = k > nst ? k - nst : 0;
     for (uint32_t c = first; c < k; ++c) {
       const uint64_t t0 = globaltimer_ns();
@@ -335,7 +331,7 @@ struct Producer {
 };
 
 template <class S>
-__device__ __noinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ring, int cta) {
+__device__ __forceinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ring, int cta) {
   if ((threadIdx.x & 31) != 0) return;
   const int N = P.ncta;
   // Its state lives in shared memory: the methods take `this`, and a stack
@@ -1116,7 +1112,7 @@ __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, u
 }
 
 template <class S>
-__device__ __noinline__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, int cta) {
+__device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, int cta) {
   const int N = P.ncta, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint32_t kc = 0;
   int tok = P.forced[0];
@@ -1350,9 +1346,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   }
   __syncthreads();
   const int cta = blockIdx.x;
-  // Out-of-line device functions read the parameters from shared memory.
-  if (threadIdx.x >= kConsumerThreads) producer<S>(sm.prm, sm, ring, cta);
-  else consumers<S>(sm.prm, sm, ring, cta);
+  // The device functions read the parameters from shared memory.  The
+  // producer warpgroup (one working warp) hands registers to the two
+  // consumer warpgroups.
+  if (threadIdx.x >= kConsumerThreads) {
+    setmaxnreg_dec<kProducerRegs>();
+    if (threadIdx.x < kConsumerThreads + 32) producer<S>(sm.prm, sm, ring, cta);
+  } else {
+    setmaxnreg_inc<kConsumerRegs>();
+    consumers<S>(sm.prm, sm, ring, cta);
+  }
 }
 
 template <class S>

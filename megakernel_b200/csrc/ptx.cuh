@@ -129,6 +129,11 @@ __device__ __forceinline__ void mma_bf16_16816(float& d0, float& d1, float& d2, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// ---- warpgroup register reallocation (all 128 threads of a warpgroup) -----
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 // ---- small math -------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -11,7 +11,15 @@ namespace mk {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;  // + one producer warp
+// Two consumer warpgroups plus a producer warpgroup of which only the first
+// warp works.  Nine warps would cap every thread at 168 registers (three
+// warps share a sub-partition's register file); with setmaxnreg the producer
+// warpgroup drops to kProducerRegs and the consumers rise to kConsumerRegs.
+// The split must not exceed what the launch allocates: 384 threads x 168.
+constexpr int kThreads = kConsumerThreads + 128;
+constexpr int kConsumerRegs = 232;
+constexpr int kProducerRegs = 40;
+static_assert(2 * 128 * kConsumerRegs + 128 * kProducerRegs <= kThreads * 168, "register split");
 constexpr int kRingBytes = 176 * 1024;
 constexpr int kMaxCtas = 256;
 constexpr int kRowsMax = 256;           // weight rows one CTA owns in one phase
