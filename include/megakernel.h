@@ -142,6 +142,16 @@ int megakernel_decode_noalloc(const void* d_weights, const long long* offsets, i
                               int n_forced, int n_steps, int* d_out, float* d_logits,
                               void* stream);
 
+/* ---- batched path building blocks (no reference counterpart) -------------- */
+
+/* One tcgen05 GEMM as the batched decode uses it: d_out[r][n] =
+ * sum_k d_x[r][k] * d_w[n][k] for r < rows (<= 64), with d_x fp32 [rows x K]
+ * and d_w bf16 [N x K] row-major (K, N multiples of 64).  x enters the
+ * tensor cores as two bf16 terms (hi, lo).  Allocates scratch; synchronous.
+ * Returns MK_OK or an MK_ERR_* code. */
+int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d_w, int K, int N, float* d_out,
+                            void* stream);
+
 /* ---- host-only helpers (no GPU needed) ----------------------------------- */
 
 /* Shape id matching a flat-binary offsets array, or MK_ERR_SHAPE. */

@@ -16,7 +16,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libmegakernel.so")
 HEADER = os.path.join(ROOT, "include", "megakernel.h")
 SOURCES = [os.path.join(CSRC, f) for f in ("megakernel.cu", "noalloc.cu", "decode_kernel.cuh", "ptx.cuh",
-                                                  "shapes.cuh")]
+                                                  "shapes.cuh", "batch.cu", "tc_gemm.cuh", "tc_ptx.cuh")]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
               "-shared", "-Xcompiler", "-fPIC"]
@@ -90,6 +90,7 @@ def signatures() -> dict:
         "megakernel_set_trace_detail": ([vp, vp], c_int),
         "megakernel_decode_noalloc": ([vp, llp, c_int, vp, c_int, c_int, vp, c_int, c_int, vp, vp, vp],
                                       c_int),
+        "megakernel_tc_gemm_test": ([vp, c_int, vp, c_int, c_int, vp, vp], c_int),
         "megakernel_infer_shape": ([llp, c_int], c_int),
         "megakernel_rope_table": ([c_int, ctypes.c_double, c_int, fp, fp], c_int),
         "megakernel_plan_bytes": ([c_int, c_int, c_int, llp], c_int),

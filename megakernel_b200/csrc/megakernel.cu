@@ -604,3 +604,4 @@ int megakernel_plan_bytes(int shape_id, int num_ctas, int pos, long long* bytes_
 // The allocation-free entry point lives in its own file; it is compiled in
 // this translation unit so both entry points launch the same kernel image.
 #include "noalloc.cu"
+#include "batch.cu"

@@ -1,0 +1,237 @@
+// Skinny tcgen05 GEMM for batched decode: C[64 x N] = X[64 x K] * W[N x K]^T
+// with X in fp32 and W in bf16 (the reference's gemv_* functions,
+// src/gemv.cuh:36-279, batched over up to 64 concurrent sequences).
+//
+// Operand A is 128 x K bf16: rows 0..63 are bf16(x) ("hi") and rows 64..127
+// are bf16(x - hi) ("lo") of the 64 sequences, so one M=128 MMA computes the
+// product with ~16 mantissa bits of x; the epilogue adds the two halves.
+//
+// Per CTA (persistent over 64-column output tiles, 256 threads):
+//   warp 0      TMA producer: A block (64 K x 128 rows, SW128) and two 32-row
+//               W blocks per stage into a 4-stage ring (full/empty mbarriers);
+//   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K=16 each) per
+//               stage into one of two 64-column fp32 accumulators, commits to
+//               the stage's empty barrier and, per tile, to tmem_full;
+//   warps 4..7  epilogue: tcgen05.ld of their 32-lane quarter (one thread
+//               per row), release the accumulator, add hi + lo through shared
+//               memory and call Epi::apply(tile, seq, v[64]) on 64 threads.
+// Every wait is bounded (timeout_ns); on expiry the kernel records
+// MK_ERR_TIMEOUT in *err and every role leaves its loop.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "../../include/megakernel.h"
+#include "tc_ptx.cuh"
+
+namespace mk {
+
+constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 4;
+constexpr int kTcABytes = kTcBM * kTcBK * 2;          // 16 KB
+constexpr int kTcWBytes = kTcBN * kTcBK * 2;          //  8 KB
+constexpr int kTcStageBytes = kTcABytes + kTcWBytes;  // 24 KB
+constexpr int kTcThreads = 256;
+constexpr int kTcCombStride = 65;                     // floats per row of the hi/lo combine buffer
+constexpr size_t kTcSmemBytes = 1024 + (size_t)kTcStages * kTcStageBytes + 64 * kTcCombStride * 4;
+constexpr uint32_t kTcTmemCols = 128;                 // two 64-column accumulators
+
+struct TcGemmParams {
+  const CUtensorMap* amap;  // A [128 x K] bf16, box {64, 128}, SW128
+  const CUtensorMap* wmap;  // W rows, box {64, 32}, SW128
+  int K;                    // multiple of 64
+  int ntiles;               // output tiles of 64 columns
+  int w_half_off;           // gate/up: row offset of the second matrix; 0: plain rows
+  int* err;
+  long long timeout_ns;
+};
+
+// W rows of tile t: [r0, r0+32) then [r1, r1+32).  Plain: 64t and 64t+32;
+// gate/up (w_half_off > 0): gate rows 32t, up rows w_half_off + 32t, so the
+// tile's columns are 32 gate outputs followed by the matching 32 up outputs.
+__device__ __forceinline__ void tc_tile_rows(const TcGemmParams& p, int t, int& r0, int& r1) {
+  if (p.w_half_off > 0) { r0 = 32 * t; r1 = p.w_half_off + 32 * t; }
+  else { r0 = 64 * t; r1 = 64 * t + 32; }
+}
+
+// Bounded mbarrier wait; false on timeout or when another role gave up.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const TcGemmParams& p,
+                                        volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort_flag) return false;
+      if ((long long)(globaltimer_ns() - t0) > p.timeout_ns) {
+        atomicCAS(p.err, 0, MK_ERR_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ TcGemmParams p, const __grid_constant__ typename Epi::Params ep) {
+  extern __shared__ uint8_t tc_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  float* comb = reinterpret_cast<float*>(smem + (size_t)kTcStages * kTcStageBytes);
+  __shared__ alignas(8) uint64_t full[kTcStages], empty[kTcStages], tfull[2], tempty[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) { tmem_alloc(&tmem_base_sh, kTcTmemCols); tmem_relinquish(); }
+  if (warp == 0 && lane == 0) { prefetch_tmap(p.amap); prefetch_tmap(p.wmap); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const int kblocks = p.K / kTcBK;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    uint32_t s = 0, ph = 0;
+    for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x) {
+      int r0, r1;
+      tc_tile_rows(p, t, r0, r1);
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!tc_wait(&empty[s], ph ^ 1u, p, &abort_flag)) goto done_producer;
+        uint8_t* st = smem + (size_t)s * kTcStageBytes;
+        mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+        tma_load_2d(st, p.amap, kb * kTcBK, 0, &full[s]);
+        tma_load_2d(st + kTcABytes, p.wmap, kb * kTcBK, r0, &full[s]);
+        tma_load_2d(st + kTcABytes + kTcWBytes / 2, p.wmap, kb * kTcBK, r1, &full[s]);
+        if (++s == kTcStages) { s = 0; ph ^= 1u; }
+      }
+    }
+  done_producer:;
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t idesc = tc_idesc_bf16(kTcBM, kTcBN);
+    uint32_t s = 0, ph = 0;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      if (!tc_wait(&tempty[buf], (((uint32_t)i >> 1) & 1u) ^ 1u, p, &abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(buf * kTcBN);
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!tc_wait(&full[s], ph, p, &abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + (size_t)s * kTcStageBytes);
+        const uint32_t w = a + kTcABytes;
+#pragma unroll
+        for (int kk = 0; kk < kTcBK / 16; ++kk)
+          tc_mma_bf16(d, tc_desc_sw128(a + kk * 32), tc_desc_sw128(w + kk * 32), idesc, (kb | kk) != 0);
+        tc_commit(&empty[s]);
+        if (++s == kTcStages) { s = 0; ph ^= 1u; }
+      }
+      if (!ok) break;
+      tc_commit(&tfull[buf]);
+    }
+  } else if (warp >= 4) {
+    // ---- epilogue ----
+    const int q = warp - 4;          // TMEM lane quarter = rows 32q .. 32q+31
+    const int row = 32 * q + lane;
+    int i = 0;
+    for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, ++i) {
+      const int buf = i & 1;
+      if (!tc_wait(&tfull[buf], ((uint32_t)i >> 1) & 1u, p, &abort_flag)) break;
+      tc_fence_after();
+      float v[64];
+      {
+        uint32_t r[32];
+        const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTcBN);
+        tmem_ld_32x32b_x32(ta, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
+        tmem_ld_32x32b_x32(ta + 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[32 + c] = __uint_as_float(r[c]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (q >= 2) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) comb[(row - 64) * kTcCombStride + c] = v[c];
+      }
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (q < 2) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) v[c] += comb[row * kTcCombStride + c];
+        Epi::apply(ep, t, row, v);
+      }
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcTmemCols);
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline PFN_encodeTiled tc_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+// Row-major bf16 matrix [rows x cols] -> tensor map with a {64, box_rows}
+// box and the 128-byte swizzle.  Returns false on failure.
+inline bool tc_make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  PFN_encodeTiled enc = tc_encode_fn();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15) != 0 || (cols * 2) % 16 != 0) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <class Epi>
+inline cudaError_t tc_gemm_launch(const TcGemmParams& p, const typename Epi::Params& ep, int max_ctas,
+                                  cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kTcSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int grid = p.ntiles < max_ctas ? p.ntiles : max_ctas;
+  tc_gemm_kernel<Epi><<<grid, kTcThreads, kTcSmemBytes, st>>>(p, ep);
+  return cudaGetLastError();
+}
+
+}  // namespace mk

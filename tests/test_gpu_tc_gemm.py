@@ -1,0 +1,31 @@
+"""tcgen05 GEMM of the batched path (megakernel_tc_gemm_test) against torch.
+
+x fp32 [rows x K] enters the tensor cores as bf16 hi + lo terms, W is bf16;
+the result must match x @ W^T computed in fp64 to 2e-5 of the output's
+largest magnitude (the lo term leaves ~2^-17 of x unrepresented;
+accumulation is fp32).
+"""
+import ctypes
+
+import pytest
+import torch
+
+from megakernel_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+@pytest.mark.parametrize("rows,K,N", [(64, 1024, 2048), (64, 2816, 1024), (7, 1024, 5632), (64, 64, 64)])
+def test_tc_gemm_matches_fp64(rows, K, N):
+    L = _lib.load()
+    g = torch.Generator(device="cpu").manual_seed(rows * 7 + K + N)
+    x = torch.randn(rows, K, generator=g).to(DEV)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    out = torch.zeros(rows, N, device=DEV)
+    rc = L.megakernel_tc_gemm_test(ctypes.c_void_p(x.data_ptr()), rows, ctypes.c_void_p(w.data_ptr()), K, N,
+                                   ctypes.c_void_p(out.data_ptr()), None)
+    assert rc == 0, rc
+    ref = x.double() @ w.double().t()
+    err = ((out.double() - ref).abs().max() / ref.abs().max()).item()
+    assert err < 2e-5, err
