@@ -91,6 +91,16 @@ def signatures() -> dict:
         "megakernel_decode_noalloc": ([vp, llp, c_int, vp, c_int, c_int, vp, c_int, c_int, vp, vp, vp],
                                       c_int),
         "megakernel_tc_gemm_test": ([vp, c_int, vp, c_int, c_int, vp, vp], c_int),
+        "megakernel_batch_init": ([vp, llp, c_int, c_int, c_int], vp),
+        "megakernel_batch_free": ([vp], None),
+        "megakernel_batch_size": ([vp], c_int),
+        "megakernel_batch_step": ([vp, vp, vp, vp, vp], c_int),
+        "megakernel_batch_decode_n": ([vp, vp, c_int, c_int, vp, vp], c_int),
+        "megakernel_batch_set_pos": ([vp, ip], c_int),
+        "megakernel_batch_get_pos": ([vp, ip], c_int),
+        "megakernel_batch_kv_ptr": ([vp], vp),
+        "megakernel_batch_kv_bytes": ([vp], c_ll),
+        "megakernel_batch_last_error": ([vp], c_int),
         "megakernel_infer_shape": ([llp, c_int], c_int),
         "megakernel_rope_table": ([c_int, ctypes.c_double, c_int, fp, fp], c_int),
         "megakernel_plan_bytes": ([c_int, c_int, c_int, llp], c_int),

@@ -6,10 +6,17 @@
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 
 #include "ptx.cuh"
 
 namespace mk {
+
+// Two floats -> packed bf16x2 (round to nearest even), low half first.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
 
 // ---- 2-D TMA (tiled, no multicast) -----------------------------------------
 // c0 is the innermost (contiguous) coordinate in elements; c0 * element size
