@@ -27,6 +27,7 @@ __global__ void hilo_split_kernel(const float* __restrict__ x, int rows, int K, 
 
 // Plain epilogue: out[seq][64 t + c] = v[c] for seq < rows.
 struct EpiStore {
+  static constexpr bool kCols = false;
   struct Params {
     float* out;
     int ldo;
@@ -68,6 +69,9 @@ struct BatchDev {
   const float* rope_sin;
   int* pos;              // [64] position of each sequence's next token
   int* err;
+  int* acnt;             // [64][8] attention chunk tickets (0 between layers)
+  float* ws;             // split-K partials (2 MB)
+  int* tickets;          // split-K arrival counters [64]
   int batch, max_seq, maxch;
 };
 
@@ -124,6 +128,7 @@ __global__ void bembed_kernel(BatchDev d, const __nv_bfloat16* __restrict__ emb,
 // value head t-24.  Scales by 1/rms, applies q_norm / k_norm and RoPE at the
 // sequence's position, writes q (fp32) or appends K / V (bf16) to the cache.
 struct EpiQKV {
+  static constexpr bool kCols = false;
   struct Params {
     BatchDev d;
     int l;
@@ -174,36 +179,49 @@ struct EpiQKV {
   }
 };
 
-// Residual epilogue (O and down projections): x += v, per-tile sum of
-// squares of the new x, and hi/lo of (g . x) for the next GEMM.
+// Residual epilogue (O and down projections).  Column phase (thread = column
+// c of the tile): x += v (coalesced), the new x goes back to the tile; then
+// thread = row: sum of squares of the row's 64 new values -> ssq[t][row];
+// then thread = column again: hi/lo of (g . x) into a_next.
 struct EpiResid {
+  static constexpr bool kCols = true;
   struct Params {
     BatchDev d;
     __nv_bfloat16* a_next;
     const __nv_bfloat16* g;
   };
-  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, float (&v)[64]) {
+  __device__ __forceinline__ static void apply(const Params&, int, int, float (&)[64]) {}
+  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int c) {
     const BatchDev& d = ep.d;
-    float* xr = d.x + (size_t)seq * kBH + 64 * t;
-    float ss = 0.f;
+    const int col = 64 * t + c;
+    const float g = __bfloat162float(ep.g[col]);
+    float xv[kBMax];   // all loads in flight before the first use
 #pragma unroll
-    for (int c = 0; c < 64; c += 4) {
-      float4 o = *reinterpret_cast<float4*>(xr + c);
-      o.x += v[c]; o.y += v[c + 1]; o.z += v[c + 2]; o.w += v[c + 3];
-      *reinterpret_cast<float4*>(xr + c) = o;
-      ss = fmaf(o.x, o.x, ss); ss = fmaf(o.y, o.y, ss); ss = fmaf(o.z, o.z, ss); ss = fmaf(o.w, o.w, ss);
-      put_hilo(ep.a_next, kBH, seq, 64 * t + c, __bfloat162float(ep.g[64 * t + c]) * o.x);
-      put_hilo(ep.a_next, kBH, seq, 64 * t + c + 1, __bfloat162float(ep.g[64 * t + c + 1]) * o.y);
-      put_hilo(ep.a_next, kBH, seq, 64 * t + c + 2, __bfloat162float(ep.g[64 * t + c + 2]) * o.z);
-      put_hilo(ep.a_next, kBH, seq, 64 * t + c + 3, __bfloat162float(ep.g[64 * t + c + 3]) * o.w);
+    for (int r = 0; r < kBMax; ++r) xv[r] = __ldcg(d.x + (size_t)r * kBH + col);
+#pragma unroll
+    for (int r = 0; r < kBMax; ++r) {
+      const float xn = xv[r] + tile[r * kTcCombStride + c];
+      __stcg(d.x + (size_t)r * kBH + col, xn);
+      tile[r * kTcCombStride + c] = xn;
+      put_hilo(ep.a_next, kBH, r, col, g * xn);
     }
-    d.ssq[t * kBMax + seq] = ss;
+    asm volatile("bar.sync 3, 64;" ::: "memory");
+    const int row = c;
+    float ss = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < 64; ++k) {
+      const float xv = tile[row * kTcCombStride + k];
+      ss = fmaf(xv, xv, ss);
+    }
+    d.ssq[t * kBMax + row] = ss;
   }
 };
 
 // Gate/up epilogue: columns 0..31 are gate rows 32t.., 32..63 the matching
-// up rows; h = silu(gate / rms) * (up / rms) -> hi/lo into a_h.
+// up rows.  Row phase: h = silu(gate / rms) * (up / rms) into v[0..31];
+// column phase: hi/lo of h into a_h (coalesced).
 struct EpiSwiGLU {
+  static constexpr bool kCols = true;
   struct Params {
     BatchDev d;
   };
@@ -213,15 +231,20 @@ struct EpiSwiGLU {
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
       const float gt = v[c] * r, up = v[32 + c] * r;
-      const float h = seq < d.batch ? gt / (1.f + expf(-gt)) * up : 0.f;
-      put_hilo(d.a_h, kBI, seq, 32 * t + c, h);
+      v[c] = seq < d.batch ? gt / (1.f + expf(-gt)) * up : 0.f;
     }
+  }
+  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid) {
+    const int c = tid & 31;
+#pragma unroll 4
+    for (int r = tid >> 5; r < kBMax; r += 2) put_hilo(ep.d.a_h, kBI, r, 32 * t + c, tile[r * kTcCombStride + c]);
   }
 };
 
 // LM-head epilogue: logits of 64 vocabulary rows; per sequence the best
 // (value, lowest index) of the tile -> lm_part[t][seq]; optional logits.
 struct EpiArgmax {
+  static constexpr bool kCols = false;
   struct Params {
     BatchDev d;
     float* logits;  // [batch][V] or null
@@ -246,115 +269,271 @@ struct EpiArgmax {
   }
 };
 
-// Split-KV attention, one warp per item (sequence b, KV head h, chunk c of
-// 64 positions <= pos_b).  Lane = two positions for the scores, two output
-// dimensions for P.V.  Writes {acc[2][64], m[2], l[2]} for the GQA pair of
-// query heads (2h, 2h+1) to part[b][h][c].  Replaces warp_attention
-// (src/attention.cuh:100-167) for many sequences at once.
-__global__ void __launch_bounds__(256) battn_kernel(BatchDev d, int l) {
-  const int lane = threadIdx.x & 31;
-  const int wglob = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int nw = gridDim.x * (blockDim.x >> 5);
-  const int nitems = d.batch * kBNKV * d.maxch;
+// Split-KV attention on tensor cores, one warp per item (sequence b, KV head
+// h, chunk c of 64 positions <= pos_b) for the GQA pair of query heads
+// (2h, 2h+1).  Replaces warp_attention (src/attention.cuh:100-167) for many
+// sequences at once.
+//   - K and V of the chunk go to this warp's shared memory with cp.async
+//     (64 rows of 128 B each, 16-byte chunks XOR-swizzled by row so ldmatrix
+//     is bank-conflict free); rows past pos are copied too but masked;
+//   - S = Q K^T and O = P V run as mma.sync m16n8k16 (bf16, fp32 accumulate).
+//     Q and P enter as two bf16 rows each (hi = bf16(v), lo = bf16(v - hi);
+//     rows 0/1 = hi of heads 0/1, rows 2/3 = lo) so the products keep ~16
+//     mantissa bits; the score accumulators are reused as the A operand of
+//     P V (same fragment layout);
+//   - the partial {acc[2][64], m[2], l[2]} goes to part[b][h][c]; the warp
+//     that completes the last chunk of (b, h) (ticket in acnt) merges all
+//     chunks in chunk order and writes hi/lo of the two heads' outputs into
+//     a_att -- no separate merge pass.
+constexpr int kBAttnWarps = 4;
+struct AttnWarpSmem {
+  alignas(128) __nv_bfloat16 k[kBChunk * kBD];  // 8 KB, swizzled
+  alignas(128) __nv_bfloat16 v[kBChunk * kBD];  // 8 KB, swizzled
+  alignas(16) float q[2][kBD];
+};
+constexpr size_t kBAttnSmem = sizeof(AttnWarpSmem) * kBAttnWarps;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+// byte offset of (row, 16-byte chunk) in a swizzled 64 x 128 B tile
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+// bf16 hi / lo terms of v packed as bf16x2 pairs
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat16 ha = __float2bfloat16_rn(a), hb = __float2bfloat16_rn(b);
+  hi = pack_bf16x2(__bfloat162float(ha), __bfloat162float(hb));
+  lo = pack_bf16x2(a - __bfloat162float(ha), b - __bfloat162float(hb));
+}
+
+// Merge of the chunk partials of (b, h) for both query heads: lanes load the
+// chunks' (m, l) in parallel (32 chunks per round), then every lane sums its
+// two output dimensions over the chunks with the weights broadcast by
+// shuffle, loads batched eight chunks at a time.  Fixed summation order.
+__device__ __forceinline__ void attn_merge(const BatchDev& d, int b, int h, int lane) {
+  const int nc = d.pos[b] / kBChunk + 1;
+  const float* base = d.part + ((size_t)b * kBNKV + h) * d.maxch * 132;
+  float M[2] = {-INFINITY, -INFINITY};
+  for (int c0 = 0; c0 < nc; c0 += 32) {
+    const int c = c0 + lane;
+    if (c < nc) {
+      M[0] = fmaxf(M[0], __ldcg(base + (size_t)c * 132 + 64));
+      M[1] = fmaxf(M[1], __ldcg(base + (size_t)c * 132 + 66 + 64));
+    }
+  }
+  M[0] = warp_max(M[0]);
+  M[1] = warp_max(M[1]);
+  float den[2] = {0.f, 0.f}, o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  for (int c0 = 0; c0 < nc; c0 += 32) {
+    const int c = c0 + lane;
+    float w[2] = {0.f, 0.f};
+    if (c < nc) {
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        w[g] = expf(__ldcg(base + (size_t)c * 132 + g * 66 + 64) - M[g]);
+        den[g] = fmaf(__ldcg(base + (size_t)c * 132 + g * 66 + 65), w[g], den[g]);
+      }
+    }
+    const int cnt = min(32, nc - c0);
+    for (int k0 = 0; k0 < cnt; k0 += 8) {
+      float2 a[8][2];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int cc = min(k0 + k, cnt - 1);
+#pragma unroll
+        for (int g = 0; g < 2; ++g)
+          a[k][g] = __ldcg(reinterpret_cast<const float2*>(base + (size_t)(c0 + cc) * 132 + g * 66 + 2 * lane));
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          const float wk = __shfl_sync(0xffffffffu, w[g], (k0 + k) & 31);
+          if (k0 + k < cnt) {
+            o[g][0] = fmaf(a[k][g].x, wk, o[g][0]);
+            o[g][1] = fmaf(a[k][g].y, wk, o[g][1]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const float inv = 1.f / warp_sum(den[g]);
+    const int col = (2 * h + g) * kBD + 2 * lane;
+    put_hilo(d.a_att, kBQ, b, col, o[g][0] * inv);
+    put_hilo(d.a_att, kBQ, b, col + 1, o[g][1] * inv);
+  }
+}
+
+__global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int l) {
+  extern __shared__ __align__(128) uint8_t attn_smem_raw[];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  AttnWarpSmem& sw = reinterpret_cast<AttnWarpSmem*>(attn_smem_raw)[wid];
+  const uint32_t ks = smem_u32(sw.k), vs = smem_u32(sw.v);
+  const int wglob = blockIdx.x * kBAttnWarps + wid;
+  const int nw = gridDim.x * kBAttnWarps;
+  const int nitems = kBMax * kBNKV * d.maxch;
   for (int it = wglob; it < nitems; it += nw) {
     const int c = it % d.maxch, h = (it / d.maxch) % kBNKV, b = it / (d.maxch * kBNKV);
+    if (b >= d.batch) continue;
     const int p = d.pos[b];
     const int c0 = c * kBChunk;
     if (c0 > p) continue;
     const int n = min(kBChunk, p + 1 - c0);
-    const __nv_bfloat16* Kc = d.kv + bkv_index(d, b, l, 0, h, c0);
-    const __nv_bfloat16* Vc = d.kv + bkv_index(d, b, l, 1, h, c0);
-    const float* q0 = d.q + ((size_t)b * kBNQ + 2 * h) * kBD;
-    const float* q1 = q0 + kBD;
-    // scores: lane handles positions lane and lane + 32
-    float s[2][2];
+    const __nv_bfloat16* Kc = d.kv + bkv_index(d, b, l, 0, h, 0);
+    const __nv_bfloat16* Vc = d.kv + bkv_index(d, b, l, 1, h, 0);
+    __syncwarp();   // the previous item's readers of sw are done
+    // 64 rows x 8 chunks of K and of V; rows past max_seq clamp (masked later)
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int pp = lane + 32 * j;
-      float a0 = 0.f, a1 = 0.f;
-      if (pp < n) {
-        const uint4* kr = reinterpret_cast<const uint4*>(Kc + (size_t)pp * kBD);
+    for (int k = 0; k < 16; ++k) {
+      const int idx = lane + 32 * k, row = idx >> 3, ch = idx & 7;
+      const int src_row = min(c0 + row, d.max_seq - 1);
+      cp_async16(ks + swz(row, ch), Kc + (size_t)src_row * kBD + ch * 8);
+      cp_async16(vs + swz(row, ch), Vc + (size_t)src_row * kBD + ch * 8);
+    }
+    {
+      const float* qg = d.q + ((size_t)b * kBNQ + 2 * h) * kBD;
+      *reinterpret_cast<float4*>(&sw.q[0][0] + 4 * lane) = __ldg(reinterpret_cast<const float4*>(qg) + lane);
+    }
+    __syncwarp();
+    // A fragments of Q (rows 0/1: hi of heads 0/1, rows 2/3: lo), 4 k-steps
+    uint32_t qa[4][2];   // a0 (cols 2tq..+1), a2 (cols 8+2tq..+1) for row g; rows >= 4 zero
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint4 w = __ldg(kr + k);
-          const float4 qa = __ldg(reinterpret_cast<const float4*>(q0) + 2 * k);
-          const float4 qb = __ldg(reinterpret_cast<const float4*>(q0) + 2 * k + 1);
-          const float4 ra = __ldg(reinterpret_cast<const float4*>(q1) + 2 * k);
-          const float4 rb = __ldg(reinterpret_cast<const float4*>(q1) + 2 * k + 1);
-          const float k0 = bf_lo(w.x), k1 = bf_hi(w.x), k2 = bf_lo(w.y), k3 = bf_hi(w.y);
-          const float k4 = bf_lo(w.z), k5 = bf_hi(w.z), k6 = bf_lo(w.w), k7 = bf_hi(w.w);
-          a0 = fmaf(k0, qa.x, a0); a0 = fmaf(k1, qa.y, a0); a0 = fmaf(k2, qa.z, a0); a0 = fmaf(k3, qa.w, a0);
-          a0 = fmaf(k4, qb.x, a0); a0 = fmaf(k5, qb.y, a0); a0 = fmaf(k6, qb.z, a0); a0 = fmaf(k7, qb.w, a0);
-          a1 = fmaf(k0, ra.x, a1); a1 = fmaf(k1, ra.y, a1); a1 = fmaf(k2, ra.z, a1); a1 = fmaf(k3, ra.w, a1);
-          a1 = fmaf(k4, rb.x, a1); a1 = fmaf(k5, rb.y, a1); a1 = fmaf(k6, rb.z, a1); a1 = fmaf(k7, rb.w, a1);
-        }
-        s[j][0] = a0 * 0.125f;
-        s[j][1] = a1 * 0.125f;
-      } else {
-        s[j][0] = -INFINITY;
-        s[j][1] = -INFINITY;
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t hi0 = 0, lo0 = 0, hi1 = 0, lo1 = 0;
+      if (g < 4) {
+        const float* qr = &sw.q[g & 1][kk * 16 + 2 * tq];
+        split2(qr[0], qr[1], hi0, lo0);
+        split2(qr[8], qr[9], hi1, lo1);
+      }
+      qa[kk][0] = g < 2 ? hi0 : lo0;
+      qa[kk][1] = g < 2 ? hi1 : lo1;
+      if (g >= 4) { qa[kk][0] = 0; qa[kk][1] = 0; }
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    // S[16 x 64]: 8 n-tiles of 8 positions
+    float sacc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f; }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        // matrices: (n-tile 2jp, k lo), (2jp, k hi), (2jp+1, k lo), (2jp+1, k hi)
+        const int mi = lane >> 3, r = lane & 7;
+        const int row = (2 * jp + (mi >> 1)) * 8 + r, ch = kk * 2 + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(ks + swz(row, ch), b0, b1, b2, b3);
+        mma_bf16_16816(sacc[2 * jp][0], sacc[2 * jp][1], sacc[2 * jp][2], sacc[2 * jp][3], qa[kk][0], 0u,
+                       qa[kk][1], 0u, b0, b1);
+        mma_bf16_16816(sacc[2 * jp + 1][0], sacc[2 * jp + 1][1], sacc[2 * jp + 1][2], sacc[2 * jp + 1][3],
+                       qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
       }
     }
-    float m[2], lsum[2], pr[2][2];
+    // rows 0/1 (+ rows 2/3 from lane + 8): full scores of heads 0/1 in lanes
+    // g = 0 / 1, positions 8j + 2tq, +1
+    float sc[8][2];
+    float mx = -INFINITY;
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      m[g] = warp_max(fmaxf(s[0][g], s[1][g]));
-      pr[0][g] = expf(s[0][g] - m[g]);
-      pr[1][g] = expf(s[1][g] - m[g]);
-      lsum[g] = warp_sum(pr[0][g] + pr[1][g]);
-    }
-    // P.V: lane owns dims 2*lane, 2*lane+1
-    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-    const uint32_t* vr = reinterpret_cast<const uint32_t*>(Vc) + lane;
-#pragma unroll 4
-    for (int pp = 0; pp < n; ++pp) {
-      const uint32_t w = __ldg(vr + (size_t)pp * (kBD / 2));
-      const int src = pp & 31;
-      const float p0 = __shfl_sync(0xffffffffu, pp < 32 ? pr[0][0] : pr[1][0], src);
-      const float p1 = __shfl_sync(0xffffffffu, pp < 32 ? pr[0][1] : pr[1][1], src);
-      const float v0 = bf_lo(w), v1 = bf_hi(w);
-      acc[0][0] = fmaf(p0, v0, acc[0][0]);
-      acc[0][1] = fmaf(p0, v1, acc[0][1]);
-      acc[1][0] = fmaf(p1, v0, acc[1][0]);
-      acc[1][1] = fmaf(p1, v1, acc[1][1]);
-    }
-    float* o = d.part + (((size_t)b * kBNKV + h) * d.maxch + c) * (2 * 66);
+    for (int j = 0; j < 8; ++j) {
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      *reinterpret_cast<float2*>(o + g * 66 + 2 * lane) = make_float2(acc[g][0], acc[g][1]);
-      if (lane == 0) { o[g * 66 + 64] = m[g]; o[g * 66 + 65] = lsum[g]; }
+      for (int e = 0; e < 2; ++e) {
+        const float v = sacc[j][e] + __shfl_down_sync(0xffffffffu, sacc[j][e], 8);
+        const int pos = 8 * j + 2 * tq + e;
+        sc[j][e] = pos < n ? v * 0.125f : -INFINITY;
+        mx = fmaxf(mx, sc[j][e]);
+      }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    float ls = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sc[j][e] = expf(sc[j][e] - mx);
+        ls += sc[j][e];
+      }
+    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+    // P as A operand: lanes g = 0/1 give hi of their head, lanes g = 2/3 the
+    // lo of lane - 8's probabilities, other rows zero.
+    uint32_t pa[4][2];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int j = 2 * kk + hh;
+        const float p0 = __shfl_up_sync(0xffffffffu, sc[j][0], 8), p1 = __shfl_up_sync(0xffffffffu, sc[j][1], 8);
+        uint32_t hi, lo, hi2, lo2;
+        split2(sc[j][0], sc[j][1], hi, lo);
+        split2(p0, p1, hi2, lo2);
+        pa[kk][hh] = g < 2 ? hi : (g < 4 ? lo2 : 0u);
+      }
+    }
+    // O[16 x 64]: 8 n-tiles of 8 dims, K = positions
+    float oacc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f; }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        // .trans matrices: (pos lo 8, dims 2jp), (pos hi 8, dims 2jp), (pos lo, 2jp+1), (pos hi, 2jp+1)
+        const int mi = lane >> 3, r = lane & 7;
+        const int row = kk * 16 + (mi & 1) * 8 + r, ch = 2 * jp + (mi >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vs + swz(row, ch), b0, b1, b2, b3);
+        mma_bf16_16816(oacc[2 * jp][0], oacc[2 * jp][1], oacc[2 * jp][2], oacc[2 * jp][3], pa[kk][0], 0u,
+                       pa[kk][1], 0u, b0, b1);
+        mma_bf16_16816(oacc[2 * jp + 1][0], oacc[2 * jp + 1][1], oacc[2 * jp + 1][2], oacc[2 * jp + 1][3],
+                       pa[kk][0], 0u, pa[kk][1], 0u, b2, b3);
+      }
+    }
+    // rows 0/1 + rows 2/3: lanes g = 0/1 hold head 0/1, dims 8j + 2tq, +1
+    float* o = d.part + (((size_t)b * kBNKV + h) * d.maxch + c) * 132;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v0 = oacc[j][0] + __shfl_down_sync(0xffffffffu, oacc[j][0], 8);
+      const float v1 = oacc[j][1] + __shfl_down_sync(0xffffffffu, oacc[j][1], 8);
+      if (g < 2) __stcg(reinterpret_cast<float2*>(o + g * 66 + 8 * j + 2 * tq), make_float2(v0, v1));
+    }
+    if (lane == 0 || lane == 4) {
+      const int hh = lane >> 2;
+      __stcg(o + hh * 66 + 64, mx);
+      __stcg(o + hh * 66 + 65, ls);
+    }
+    // Ticket: the warp finishing the last chunk of (b, h) merges.
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      const int nc = p / kBChunk + 1;
+      const int old = atomicAdd(d.acnt + b * kBNKV + h, 1);
+      last = old == nc - 1;
+      if (last) d.acnt[b * kBNKV + h] = 0;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence();
+      attn_merge(d, b, h, lane);
     }
   }
-}
-
-// Merge of the chunk partials of (sequence b, query head qh): one warp, lane
-// = two dims.  Writes hi/lo of the attention output into a_att.
-__global__ void __launch_bounds__(256) bmerge_kernel(BatchDev d) {
-  const int lane = threadIdx.x & 31;
-  const int wi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (wi >= kBMax * kBNQ) return;
-  const int b = wi / kBNQ, qh = wi % kBNQ, h = qh / 2, g = qh % 2;
-  float o0 = 0.f, o1 = 0.f;
-  if (b < d.batch) {
-    const int nc = d.pos[b] / kBChunk + 1;
-    const float* base = d.part + ((size_t)b * kBNKV + h) * d.maxch * (2 * 66) + g * 66;
-    float M = -INFINITY;
-    for (int c = 0; c < nc; ++c) M = fmaxf(M, base[(size_t)c * 132 + 64]);
-    float den = 0.f;
-    for (int c = 0; c < nc; ++c) {
-      const float* pc = base + (size_t)c * 132;
-      const float w = expf(pc[64] - M);
-      den = fmaf(pc[65], w, den);
-      const float2 a = *reinterpret_cast<const float2*>(pc + 2 * lane);
-      o0 = fmaf(a.x, w, o0);
-      o1 = fmaf(a.y, w, o1);
-    }
-    const float inv = 1.f / den;
-    o0 *= inv;
-    o1 *= inv;
-  }
-  put_hilo(d.a_att, kBQ, b, qh * kBD + 2 * lane, o0);
-  put_hilo(d.a_att, kBQ, b, qh * kBD + 2 * lane + 1, o1);
 }
 
 // Per-sequence argmax over the LM tiles -> out[b]; advances pos[b].
@@ -407,7 +586,7 @@ extern "C" int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d
       cudaMemcpyAsync(maps, h, sizeof(h), cudaMemcpyHostToDevice, st);
       cudaMemsetAsync(err, 0, sizeof(int), st);
       mk::hilo_split_kernel<<<64, 256, 0, st>>>(d_x, rows, K, a);
-      mk::TcGemmParams p{maps, maps + 1, K, N / 64, 0, err, 1000000000LL};
+      mk::TcGemmParams p{maps, maps + 1, K, N / 64, 0, err, 1000000000LL, 1, nullptr, nullptr};
       mk::EpiStore::Params ep{d_out, N, rows};
       if (mk::tc_gemm_launch<mk::EpiStore>(p, ep, sms, st) != cudaSuccess) rc = MK_ERR_LAUNCH;
       int herr = 0;
@@ -439,6 +618,18 @@ struct BatchState {
 };
 
 enum { kMapAx = 0, kMapAatt = 1, kMapAh = 2, kMapLayer0 = 3 };
+constexpr size_t kBWsBytes = (size_t)2 << 20;
+
+// GEMM launch parameters with K split over `ksplit` CTAs per output tile
+// (every split keeps at least one K block; partials fit the workspace).
+mk::TcGemmParams gemm_params(const mk::BatchDev& d, const CUtensorMap* a, const CUtensorMap* w, int K, int ntiles,
+                             int half_off, int ksplit) {
+  const int kb = K / mk::kTcBK;
+  while (ksplit > 1 && ((ksplit - 1) * ((kb + ksplit - 1) / ksplit) >= kb ||
+                        (size_t)ntiles * ksplit * 64 * 64 * 4 > kBWsBytes || ntiles > 64))
+    --ksplit;
+  return mk::TcGemmParams{a, w, K, ntiles, half_off, d.err, 1000000000LL, ksplit, d.ws, d.tickets};
+}
 inline int map_layer(int l, int k) { return kMapLayer0 + 4 * l + k; }   // k: 0 qkv, 1 o, 2 gate/up, 3 down
 inline int map_lm() { return kMapLayer0 + 4 * mk::kBL; }
 
@@ -447,7 +638,7 @@ void batch_free(BatchState* s) {
   cudaFree(s->d.x); cudaFree(s->d.ssq); cudaFree(s->d.a_x); cudaFree(s->d.a_att); cudaFree(s->d.a_h);
   cudaFree(s->d.q); cudaFree(s->d.part); cudaFree(s->d.lm_part); cudaFree(s->d.kv);
   cudaFree(const_cast<float*>(s->d.rope_cos)); cudaFree(const_cast<float*>(s->d.rope_sin));
-  cudaFree(s->d.pos); cudaFree(s->d.err); cudaFree(s->maps);
+  cudaFree(s->d.pos); cudaFree(s->d.err); cudaFree(s->maps); cudaFree(s->d.ws); cudaFree(s->d.tickets); cudaFree(s->d.acnt);
   delete s;
 }
 
@@ -493,7 +684,9 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
       balloc(&d.lm_part, sizeof(unsigned long long) * (size_t)kBLMTiles * kBMax) &&
       balloc(&d.kv, (size_t)s->kv_bytes) && balloc(&rc, sizeof(float) * (size_t)max_seq * 32) &&
       balloc(&rs, sizeof(float) * (size_t)max_seq * 32) && balloc(&d.pos, sizeof(int) * kBMax) &&
-      balloc(&d.err, sizeof(int) * 4) && balloc(&s->maps, sizeof(CUtensorMap) * (map_lm() + 1));
+      balloc(&d.err, sizeof(int) * 4) && balloc(&s->maps, sizeof(CUtensorMap) * (map_lm() + 1)) &&
+      balloc(&d.ws, kBWsBytes) && balloc(&d.tickets, sizeof(int) * 64) &&
+      balloc(&d.acnt, sizeof(int) * kBMax * kBNKV);
   d.rope_cos = rc;
   d.rope_sin = rs;
   if (!ok) { batch_free(s); return nullptr; }
@@ -529,29 +722,34 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
 int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, float* logits, cudaStream_t st) {
   using namespace mk;
   const BatchDev& d = s->d;
-  const long long to = 1000000000LL;
   const CUtensorMap* M = s->maps;
   bembed_kernel<<<kBMax, 256, 0, st>>>(d, s->wp[0], s->wp[2], forced, prev_out);
-  const int attn_blocks = s->sms * 4;
+  const int attn_blocks = s->sms * 3;   // 3 blocks of 4 warps (3 x 66 KB of shared memory) per SM
+  static bool attn_attr = false;
+  if (!attn_attr) {
+    if (cudaFuncSetAttribute(battn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBAttnSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(battn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+      return ::MK_ERR_LAUNCH;
+    attn_attr = true;
+  }
   for (int l = 0; l < kBL; ++l) {
     const int b = 2 + 11 * l;
     const __nv_bfloat16* g_next = l + 1 < kBL ? s->wp[b + 11] : s->wp[1];
-    if (tc_gemm_launch<EpiQKV>(TcGemmParams{M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, d.err, to},
+    if (tc_gemm_launch<EpiQKV>(gemm_params(d, M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, 4),
                                EpiQKV::Params{d, l, s->wp[b + 4], s->wp[b + 5]}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    battn_kernel<<<attn_blocks, 256, 0, st>>>(d, l);
-    bmerge_kernel<<<(kBMax * kBNQ * 32 + 255) / 256, 256, 0, st>>>(d);
-    if (tc_gemm_launch<EpiResid>(TcGemmParams{M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, d.err, to},
+    battn_kernel<<<attn_blocks, kBAttnWarps * 32, kBAttnSmem, st>>>(d, l);
+    if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, 8),
                                  EpiResid::Params{d, d.a_x, s->wp[b + 7]}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (tc_gemm_launch<EpiSwiGLU>(TcGemmParams{M + kMapAx, M + map_layer(l, 2), kBH, kBI / 32, kBI, d.err, to},
+    if (tc_gemm_launch<EpiSwiGLU>(gemm_params(d, M + kMapAx, M + map_layer(l, 2), kBH, kBI / 32, kBI, 1),
                                   EpiSwiGLU::Params{d}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (tc_gemm_launch<EpiResid>(TcGemmParams{M + kMapAh, M + map_layer(l, 3), kBI, kBH / 64, 0, d.err, to},
+    if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAh, M + map_layer(l, 3), kBI, kBH / 64, 0, 8),
                                  EpiResid::Params{d, d.a_x, g_next}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
   }
-  if (tc_gemm_launch<EpiArgmax>(TcGemmParams{M + kMapAx, M + map_lm(), kBH, kBLMTiles, 0, d.err, to},
+  if (tc_gemm_launch<EpiArgmax>(gemm_params(d, M + kMapAx, M + map_lm(), kBH, kBLMTiles, 0, 1),
                                 EpiArgmax::Params{d, logits}, s->sms, st) != cudaSuccess)
     return ::MK_ERR_LAUNCH;
   bargmax_kernel<<<s->batch, 256, 0, st>>>(d, out);

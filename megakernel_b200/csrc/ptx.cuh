@@ -108,6 +108,18 @@ __device__ __forceinline__ bool consumer_any(int nthreads, bool pred) {
   return r != 0;
 }
 
+// Named barrier `id` over n threads that ORs a predicate (same result in all).
+__device__ __forceinline__ bool bar_any(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(nthreads) : "memory");
+  return r != 0;
+}
+
 // ---- warp-level tensor-core GEMV pieces -----------------------------------
 __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& a0, uint32_t& a1, uint32_t& a2,
                                             uint32_t& a3) {

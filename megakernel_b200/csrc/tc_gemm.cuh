@@ -14,7 +14,11 @@
 //               the stage's empty barrier and, per tile, to tmem_full;
 //   warps 4..7  epilogue: tcgen05.ld of their 32-lane quarter (one thread
 //               per row), release the accumulator, add hi + lo through shared
-//               memory and call Epi::apply(tile, seq, v[64]) on 64 threads.
+//               memory, (split K) publish / collect the parts, then
+//               Epi::apply(ep, tile, seq, v[64]) on 64 threads (one per row)
+//               and, when Epi::kCols, Epi::cols(ep, tile, smem_tile, c) with
+//               the 64 x 64 tile in shared memory and one thread per column,
+//               so global writes are coalesced.
 // Every wait is bounded (timeout_ns); on expiry the kernel records
 // MK_ERR_TIMEOUT in *err and every role leaves its loop.
 #pragma once
@@ -45,6 +49,9 @@ struct TcGemmParams {
   int w_half_off;           // gate/up: row offset of the second matrix; 0: plain rows
   int* err;
   long long timeout_ns;
+  int ksplit;               // K blocks split over this many CTAs per tile (1: no split)
+  float* ws;                // split partials [ntiles][ksplit][64][64] (ksplit > 1)
+  int* counters;            // [ntiles] arrival tickets, 0 between launches (ksplit > 1)
 };
 
 // W rows of tile t: [r0, r0+32) then [r1, r1+32).  Plain: 64t and 64t+32;
@@ -97,14 +104,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
   const int kblocks = p.K / kTcBK;
+  const int kper = (kblocks + p.ksplit - 1) / p.ksplit;   // K blocks per split
+  const int nunits = p.ntiles * p.ksplit;
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
     uint32_t s = 0, ph = 0;
-    for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x) {
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+      const int t = u / p.ksplit, sp = u % p.ksplit;
       int r0, r1;
       tc_tile_rows(p, t, r0, r1);
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = sp * kper; kb < min(kblocks, (sp + 1) * kper); ++kb) {
         if (!tc_wait(&empty[s], ph ^ 1u, p, &abort_flag)) goto done_producer;
         uint8_t* st = smem + (size_t)s * kTcStageBytes;
         mbar_arrive_expect_tx(&full[s], kTcStageBytes);
@@ -120,20 +130,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr uint32_t idesc = tc_idesc_bf16(kTcBM, kTcBN);
     uint32_t s = 0, ph = 0;
     int i = 0;
-    for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, ++i) {
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
+      const int sp = u % p.ksplit;
+      const int kb0 = sp * kper, kb1 = min(kblocks, (sp + 1) * kper);
       const int buf = i & 1;
       if (!tc_wait(&tempty[buf], (((uint32_t)i >> 1) & 1u) ^ 1u, p, &abort_flag)) break;
       tc_fence_after();
       const uint32_t d = tmem + (uint32_t)(buf * kTcBN);
       bool ok = true;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc_wait(&full[s], ph, p, &abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a = smem_u32(smem + (size_t)s * kTcStageBytes);
         const uint32_t w = a + kTcABytes;
 #pragma unroll
         for (int kk = 0; kk < kTcBK / 16; ++kk)
-          tc_mma_bf16(d, tc_desc_sw128(a + kk * 32), tc_desc_sw128(w + kk * 32), idesc, (kb | kk) != 0);
+          tc_mma_bf16(d, tc_desc_sw128(a + kk * 32), tc_desc_sw128(w + kk * 32), idesc, (kb > kb0) || kk != 0);
         tc_commit(&empty[s]);
         if (++s == kTcStages) { s = 0; ph ^= 1u; }
       }
@@ -144,10 +156,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- epilogue ----
     const int q = warp - 4;          // TMEM lane quarter = rows 32q .. 32q+31
     const int row = 32 * q + lane;
+    float* tile = comb;              // [64][kTcCombStride]: lo half, then the final tile
+    __shared__ int last_flag;
     int i = 0;
-    for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, ++i) {
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
+      const int t = u / p.ksplit, sp = u % p.ksplit;
       const int buf = i & 1;
-      if (!tc_wait(&tfull[buf], ((uint32_t)i >> 1) & 1u, p, &abort_flag)) break;
+      // All four epilogue warps leave together (they share named barriers).
+      if (bar_any(2, 128, !tc_wait(&tfull[buf], ((uint32_t)i >> 1) & 1u, p, &abort_flag))) break;
       tc_fence_after();
       float v[64];
       {
@@ -167,13 +183,54 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[buf]);
       if (q >= 2) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) comb[(row - 64) * kTcCombStride + c] = v[c];
+        for (int c = 0; c < 64; ++c) tile[(row - 64) * kTcCombStride + c] = v[c];
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
+      bool do_epi = true;
       if (q < 2) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) v[c] += comb[row * kTcCombStride + c];
+        for (int c = 0; c < 64; ++c) v[c] += tile[row * kTcCombStride + c];
+        if (p.ksplit > 1) {
+          // Split K: publish this part, take a ticket; the last part's CTA
+          // sums all parts in split order (deterministic) and finishes.
+          float* wsr = p.ws + (((size_t)t * p.ksplit + sp) * 64 + row) * 64;
+#pragma unroll
+          for (int c = 0; c < 64; c += 4) __stcg(reinterpret_cast<float4*>(wsr + c), make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]));
+          __threadfence();
+          asm volatile("bar.sync 3, 64;" ::: "memory");
+          if (row == 0) {
+            const int old = atomicAdd(p.counters + t, 1);
+            last_flag = (old == p.ksplit - 1);
+            if (old == p.ksplit - 1) p.counters[t] = 0;
+          }
+          asm volatile("bar.sync 3, 64;" ::: "memory");
+          do_epi = last_flag != 0;
+          if (do_epi) {
+            __threadfence();
+#pragma unroll
+            for (int c = 0; c < 64; ++c) v[c] = 0.f;
+            for (int k = 0; k < p.ksplit; ++k) {
+              const float* pr = p.ws + (((size_t)t * p.ksplit + k) * 64 + row) * 64;
+#pragma unroll
+              for (int c = 0; c < 64; c += 4) {
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(pr + c));
+                v[c] += a.x; v[c + 1] += a.y; v[c + 2] += a.z; v[c + 3] += a.w;
+              }
+            }
+          }
+        }
+      }
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (q < 2 && do_epi) {
         Epi::apply(ep, t, row, v);
+        // Column phase: the row values go through shared memory so that
+        // global writes are coalesced (lanes = consecutive columns).
+        if constexpr (Epi::kCols) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) tile[row * kTcCombStride + c] = v[c];
+          asm volatile("bar.sync 3, 64;" ::: "memory");
+          Epi::cols(ep, t, tile, row);
+        }
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
     }
@@ -229,7 +286,8 @@ inline cudaError_t tc_gemm_launch(const TcGemmParams& p, const typename Epi::Par
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int grid = p.ntiles < max_ctas ? p.ntiles : max_ctas;
+  const int units = p.ntiles * p.ksplit;
+  const int grid = units < max_ctas ? units : max_ctas;
   tc_gemm_kernel<Epi><<<grid, kTcThreads, kTcSmemBytes, st>>>(p, ep);
   return cudaGetLastError();
 }
