@@ -103,6 +103,8 @@ __global__ void bembed_kernel(BatchDev d, const __nv_bfloat16* __restrict__ emb,
                               const int* __restrict__ forced, const int* __restrict__ prev_out) {
   const int b = blockIdx.x;
   __shared__ float red[32];
+  pdl_launch();
+  pdl_wait();
   if (b >= kBMax) return;
   float ss = 0.f;
   const bool live = b < d.batch;
@@ -387,6 +389,8 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
   const int wglob = blockIdx.x * kBAttnWarps + wid;
   const int nw = gridDim.x * kBAttnWarps;
   const int nitems = kBMax * kBNKV * d.maxch;
+  pdl_launch();
+  pdl_wait();
   for (int it = wglob; it < nitems; it += nw) {
     const int c = it % d.maxch, h = (it / d.maxch) % kBNKV, b = it / (d.maxch * kBNKV);
     if (b >= d.batch) continue;
@@ -540,6 +544,8 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
 __global__ void bargmax_kernel(BatchDev d, int* __restrict__ out) {
   const int b = blockIdx.x;
   __shared__ unsigned long long red[32];
+  pdl_launch();
+  pdl_wait();
   unsigned long long best = 0;
   for (int t = threadIdx.x; t < kBLMTiles; t += blockDim.x) {
     const unsigned long long k = d.lm_part[(size_t)t * kBMax + b];
@@ -719,11 +725,29 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
 
 // One step for every sequence: input tokens from `forced` (device, [batch])
 // or, when null, from `prev_out`; next tokens to `out`; optional logits.
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous one drains; it calls griddepcontrol.wait before reading it.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, float* logits, cudaStream_t st) {
   using namespace mk;
   const BatchDev& d = s->d;
   const CUtensorMap* M = s->maps;
-  bembed_kernel<<<kBMax, 256, 0, st>>>(d, s->wp[0], s->wp[2], forced, prev_out);
+  if (launch_pdl(bembed_kernel, kBMax, 256, 0, st, d, s->wp[0], s->wp[2], forced, prev_out) != cudaSuccess)
+    return ::MK_ERR_LAUNCH;
   const int attn_blocks = s->sms * 3;   // 3 blocks of 4 warps (3 x 66 KB of shared memory) per SM
   static bool attn_attr = false;
   if (!attn_attr) {
@@ -738,7 +762,8 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
     if (tc_gemm_launch<EpiQKV>(gemm_params(d, M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, 4),
                                EpiQKV::Params{d, l, s->wp[b + 4], s->wp[b + 5]}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    battn_kernel<<<attn_blocks, kBAttnWarps * 32, kBAttnSmem, st>>>(d, l);
+    if (launch_pdl(battn_kernel, attn_blocks, kBAttnWarps * 32, kBAttnSmem, st, d, l) != cudaSuccess)
+      return ::MK_ERR_LAUNCH;
     if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, 8),
                                  EpiResid::Params{d, d.a_x, s->wp[b + 7]}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
@@ -752,7 +777,7 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
   if (tc_gemm_launch<EpiArgmax>(gemm_params(d, M + kMapAx, M + map_lm(), kBH, kBLMTiles, 0, 1),
                                 EpiArgmax::Params{d, logits}, s->sms, st) != cudaSuccess)
     return ::MK_ERR_LAUNCH;
-  bargmax_kernel<<<s->batch, 256, 0, st>>>(d, out);
+  if (launch_pdl(bargmax_kernel, s->batch, 256, 0, st, d, out) != cudaSuccess) return ::MK_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? ::MK_OK : ::MK_ERR_LAUNCH;
 }
 

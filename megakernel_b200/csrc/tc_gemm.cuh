@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   if (warp == 1) { tmem_alloc(&tmem_base_sh, kTcTmemCols); tmem_relinquish(); }
   if (warp == 0 && lane == 0) { prefetch_tmap(p.amap); prefetch_tmap(p.wmap); }
+  pdl_launch();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -109,18 +110,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
+    // Weights do not depend on the previous kernel: the W blocks of the first
+    // stages are requested before waiting for it; A (its output) after.
+    const int u0 = blockIdx.x;
+    int pre = 0;
+    if (u0 < nunits) {
+      const int t = u0 / p.ksplit, sp = u0 % p.ksplit;
+      int r0, r1;
+      tc_tile_rows(p, t, r0, r1);
+      const int kb0 = sp * kper, kb1 = min(kblocks, (sp + 1) * kper);
+      pre = min(kTcStages, kb1 - kb0);
+      for (int j = 0; j < pre; ++j) {
+        uint8_t* st = smem + (size_t)j * kTcStageBytes;
+        mbar_arrive_expect_tx(&full[j], kTcStageBytes);
+        tma_load_2d(st + kTcABytes, p.wmap, (kb0 + j) * kTcBK, r0, &full[j]);
+        tma_load_2d(st + kTcABytes + kTcWBytes / 2, p.wmap, (kb0 + j) * kTcBK, r1, &full[j]);
+      }
+    }
+    pdl_wait();
     uint32_t s = 0, ph = 0;
+    int issued = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
       const int t = u / p.ksplit, sp = u % p.ksplit;
       int r0, r1;
       tc_tile_rows(p, t, r0, r1);
-      for (int kb = sp * kper; kb < min(kblocks, (sp + 1) * kper); ++kb) {
-        if (!tc_wait(&empty[s], ph ^ 1u, p, &abort_flag)) goto done_producer;
+      for (int kb = sp * kper; kb < min(kblocks, (sp + 1) * kper); ++kb, ++issued) {
         uint8_t* st = smem + (size_t)s * kTcStageBytes;
-        mbar_arrive_expect_tx(&full[s], kTcStageBytes);
-        tma_load_2d(st, p.amap, kb * kTcBK, 0, &full[s]);
-        tma_load_2d(st + kTcABytes, p.wmap, kb * kTcBK, r0, &full[s]);
-        tma_load_2d(st + kTcABytes + kTcWBytes / 2, p.wmap, kb * kTcBK, r1, &full[s]);
+        if (issued < pre) {
+          tma_load_2d(st, p.amap, kb * kTcBK, 0, &full[s]);
+        } else {
+          if (!tc_wait(&empty[s], ph ^ 1u, p, &abort_flag)) goto done_producer;
+          mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+          tma_load_2d(st, p.amap, kb * kTcBK, 0, &full[s]);
+          tma_load_2d(st + kTcABytes, p.wmap, kb * kTcBK, r0, &full[s]);
+          tma_load_2d(st + kTcABytes + kTcWBytes / 2, p.wmap, kb * kTcBK, r1, &full[s]);
+        }
         if (++s == kTcStages) { s = 0; ph ^= 1u; }
       }
     }
@@ -158,6 +182,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int row = 32 * q + lane;
     float* tile = comb;              // [64][kTcCombStride]: lo half, then the final tile
     __shared__ int last_flag;
+    pdl_wait();                      // epilogues read the previous kernel's outputs
     int i = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
       const int t = u / p.ksplit, sp = u % p.ksplit;
@@ -288,7 +313,18 @@ inline cudaError_t tc_gemm_launch(const TcGemmParams& p, const typename Epi::Par
   }
   const int units = p.ntiles * p.ksplit;
   const int grid = units < max_ctas ? units : max_ctas;
-  tc_gemm_kernel<Epi><<<grid, kTcThreads, kTcSmemBytes, st>>>(p, ep);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Epi>, p, ep);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -18,6 +18,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// ---- programmatic dependent launch -----------------------------------------
+// wait: block until the preceding kernel in the stream has completed and its
+// writes are visible; launch_dependents: let the next kernel start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- 2-D TMA (tiled, no multicast) -----------------------------------------
 // c0 is the innermost (contiguous) coordinate in elements; c0 * element size
 // must be a multiple of 16 bytes.

@@ -1,0 +1,79 @@
+"""Batched decode (megakernel_batch_*: up to 64 sequences per step, tcgen05
+GEMMs) against the fp32 oracle, per sequence.
+
+Gates as for the single-stream path: logits within
+2e-2 max-abs of the fp32 reference, argmax equal wherever the reference's
+top-2 margin exceeds 1e-2.  The oracle runs each sequence alone (same
+weights, same tokens, bf16 K/V), which is what a batched decode must
+reproduce.
+"""
+import numpy as np
+import pytest
+import torch
+
+from megakernel_b200.batch import BatchDecoder
+from oracle.qwen3_decode import Qwen3DecodeOracle
+
+from ._common import LOGIT_TOL, MARGIN, weights
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _tokens(batch, steps, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, 151936, (batch, steps), generator=g)
+
+
+def _run_forced(bd, toks):
+    lgs, outs = [], []
+    for t in range(toks.shape[1]):
+        out, lg = bd.step(toks[:, t].to(DEV), logits=True)
+        lgs.append(lg.cpu().numpy())
+        outs.append(out.cpu().numpy())
+    return np.stack(lgs, 1), np.stack(outs, 1)
+
+
+def _check_seq(shape, w, seq, lg, out):
+    o = Qwen3DecodeOracle(shape, w, kv_bf16=True, max_seq=64, device="cuda")
+    ot, ol, om = o.run(seq, len(seq))
+    assert np.abs(lg - ol).max() < LOGIT_TOL, np.abs(lg - ol).max()
+    ok = om > MARGIN
+    assert np.array_equal(out[ok], ot[ok])
+
+
+def test_batch_teacher_forced_vs_oracle():
+    shape, w, flat, offs = weights("qwen3-0.6b-d64")
+    toks = _tokens(4, 6)
+    bd = BatchDecoder(flat, offs, batch=4, max_seq=128)
+    lg, out = _run_forced(bd, toks)
+    assert bd.pos == [6] * 4
+    for b in range(4):
+        _check_seq(shape, w, toks[b].tolist(), lg[b], out[b])
+    bd.close()
+
+
+def test_batch_full_64_vs_oracle():
+    shape, w, flat, offs = weights("qwen3-0.6b-d64")
+    toks = _tokens(64, 3, seed=5)
+    bd = BatchDecoder(flat, offs, batch=64, max_seq=96)
+    lg, out = _run_forced(bd, toks)
+    for b in (0, 31, 63):
+        _check_seq(shape, w, toks[b].tolist(), lg[b], out[b])
+    bd.close()
+
+
+def test_batch_decode_n_equals_steps():
+    """One decode_n call (forced prefix, then greedy) == step-by-step calls; bit-exact."""
+    shape, w, flat, offs = weights("qwen3-0.6b-d64")
+    toks = _tokens(8, 3, seed=7).to(DEV, torch.int32)
+    bd = BatchDecoder(flat, offs, batch=8, max_seq=64)
+    out_n = bd.decode_n(toks.t().contiguous(), 7).cpu().numpy()
+    bd.reset()
+    ref, cur = [], None
+    for t in range(7):
+        cur = bd.step(toks[:, t] if t < 3 else cur)
+        ref.append(cur.cpu().numpy())
+    assert np.array_equal(out_n, np.stack(ref, 0))
+    assert bd.pos == [7] * 8
+    bd.close()

@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
-@pytest.mark.parametrize("rows,K,N", [(64, 1024, 2048), (64, 2816, 1024), (7, 1024, 5632), (64, 64, 64)])
+@pytest.mark.parametrize("rows,K,N", [(64, 1024, 2048), (64, 2816, 1024), (7, 1024, 5632), (64, 64, 64), (64, 4096, 128)])
 def test_tc_gemm_matches_fp64(rows, K, N):
     L = _lib.load()
     g = torch.Generator(device="cpu").manual_seed(rows * 7 + K + N)
