@@ -152,6 +152,30 @@ int megakernel_decode_noalloc(const void* d_weights, const long long* offsets, i
 int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d_w, int K, int N, float* d_out,
                             void* stream);
 
+/* ---- batched decode (no reference counterpart) ----------------------------
+ * Up to 64 sequences advance together, one token each per step, each at its
+ * own position; matrix products run on tcgen05 tensor cores with the
+ * sequences as the M dimension.  Same flat weights + offsets as
+ * megakernel_init (d64 shape only).  KV layout: [batch][L][2][KVH][max_seq][hd]
+ * bf16, i.e. one reference-layout cache (src/kv_cache.cuh:9-32) per sequence.
+ * Positions start at 0; every step advances every sequence by one. */
+void* megakernel_batch_init(const void* d_weights, const long long* offsets, int num_offsets, int batch,
+                            int max_seq);
+void megakernel_batch_free(void* handle);
+int megakernel_batch_size(void* handle);
+/* One step: d_tokens[batch] (device) -> d_out[batch] next greedy tokens;
+ * d_logits (device, [batch][vocab] fp32) may be NULL.  Synchronous. */
+int megakernel_batch_step(void* handle, const int* d_tokens, int* d_out, float* d_logits, void* stream);
+/* n_steps steps: step t < n_forced consumes d_forced[t][batch], later steps
+ * consume the previous step's outputs; d_out[n_steps][batch].  Synchronous. */
+int megakernel_batch_decode_n(void* handle, const int* d_forced, int n_forced, int n_steps, int* d_out,
+                              void* stream);
+int megakernel_batch_set_pos(void* handle, const int* h_pos);   /* h_pos[batch] */
+int megakernel_batch_get_pos(void* handle, int* h_pos);
+void* megakernel_batch_kv_ptr(void* handle);
+long long megakernel_batch_kv_bytes(void* handle);
+int megakernel_batch_last_error(void* handle);
+
 /* ---- host-only helpers (no GPU needed) ----------------------------------- */
 
 /* Shape id matching a flat-binary offsets array, or MK_ERR_SHAPE. */
