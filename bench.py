@@ -38,8 +38,8 @@ METRIC = "decode tok/s, Qwen3-0.6B shape, B=1 on 1×B200; % of HBM roofline"
 PROMPT, GEN = 128, 512
 # DRAM bytes (read + write) per decoded token of the decode kernel, from the
 # ncu capture summarised in profiles/decode_kernel_d64_b1.md (2-step launch
-# at positions 0-1: 1.944 GB read + 7.7 MB written per 2 tokens, per token).
-NCU_TRAFFIC_PER_TOKEN = 975_960_000
+# at positions 0-1: 1.944 GB read + 4.0 MB written per 2 tokens, per token).
+NCU_TRAFFIC_PER_TOKEN = 973_941_000
 
 
 def load_peaks():
