@@ -152,6 +152,15 @@ int megakernel_decode_noalloc(const void* d_weights, const long long* offsets, i
 int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d_w, int K, int N, float* d_out,
                             void* stream);
 
+/* Parallel prefill (no reference counterpart; replaces the token-serial
+ * prompt loop of host/bridge.py:158-162): feeds d_tokens[n_tokens] (device)
+ * at positions pos .. pos+n-1 of this engine's cache, 64 positions per
+ * batched tcgen05 step, advances pos by n and writes the greedy token after
+ * the last prompt token to d_next (device).  Graded (head_dim 64) shape
+ * only (MK_ERR_SHAPE otherwise); synchronous.  megakernel_generate uses it
+ * for that shape (set MK_SERIAL_PREFILL to force the token-serial loop). */
+int megakernel_prefill(void* handle, const int* d_tokens, int n_tokens, int* d_next, void* stream);
+
 /* ---- batched decode (no reference counterpart) ----------------------------
  * Up to 64 sequences advance together, one token each per step, each at its
  * own position; matrix products run on tcgen05 tensor cores with the

@@ -201,6 +201,17 @@ class MegakernelEngine:
         _lib.check(rc, "megakernel_decode_n")
         return out
 
+    def prefill(self, tokens: torch.Tensor, stream=None) -> torch.Tensor:
+        """Parallel prefill (megakernel_prefill): feed the int32 device tensor
+        `tokens` at the current position, 64 positions per batched tcgen05
+        step; returns the greedy next token as a 1-element device tensor."""
+        assert tokens.dtype == torch.int32 and tokens.is_contiguous()
+        nxt = torch.empty(1, dtype=torch.int32, device=tokens.device)
+        st = stream.cuda_stream if stream is not None else None
+        rc = self.lib.megakernel_prefill(self._handle, tokens.data_ptr(), int(tokens.numel()), nxt.data_ptr(), st)
+        _lib.check(rc, "megakernel_prefill")
+        return nxt
+
     def set_logits_capture(self, enable=True):
         _lib.check(self.lib.megakernel_set_logits_capture(self._handle, int(enable)))
 

@@ -73,10 +73,12 @@ struct BatchDev {
   float* ws;             // split-K partials (2 MB)
   int* tickets;          // split-K arrival counters [64]
   int batch, max_seq, maxch;
+  int seq_mode;          // 0: row b is sequence b; 1: every row belongs to sequence 0 (prefill)
 };
 
 __device__ __forceinline__ size_t bkv_index(const BatchDev& d, int b, int l, int kv, int h, int p) {
-  return (((((size_t)b * kBL + l) * 2 + kv) * kBNKV + h) * (size_t)d.max_seq + p) * kBD;
+  const size_t sq = d.seq_mode ? 0 : (size_t)b;
+  return ((((sq * kBL + l) * 2 + kv) * kBNKV + h) * (size_t)d.max_seq + p) * kBD;
 }
 // 1 / rms of row `seq` of x from the 16 tile partials (fixed order).
 __device__ __forceinline__ float inv_rms(const float* ssq, int seq) {
@@ -621,6 +623,8 @@ struct BatchState {
   CUtensorMap* maps = nullptr;   // device copy: [0] a_x, [1] a_att, [2] a_h, [3 + 4l + k] layer maps, [3 + 4L] LM
   int last_error = 0;
   long long kv_bytes = 0;
+  bool owns_kv = true;
+  int* d_tmp = nullptr;          // [64] scratch tokens (prefill)
 };
 
 enum { kMapAx = 0, kMapAatt = 1, kMapAh = 2, kMapLayer0 = 3 };
@@ -642,7 +646,9 @@ inline int map_lm() { return kMapLayer0 + 4 * mk::kBL; }
 void batch_free(BatchState* s) {
   if (!s) return;
   cudaFree(s->d.x); cudaFree(s->d.ssq); cudaFree(s->d.a_x); cudaFree(s->d.a_att); cudaFree(s->d.a_h);
-  cudaFree(s->d.q); cudaFree(s->d.part); cudaFree(s->d.lm_part); cudaFree(s->d.kv);
+  cudaFree(s->d.q); cudaFree(s->d.part); cudaFree(s->d.lm_part);
+  if (s->owns_kv) cudaFree(s->d.kv);
+  cudaFree(s->d_tmp);
   cudaFree(const_cast<float*>(s->d.rope_cos)); cudaFree(const_cast<float*>(s->d.rope_sin));
   cudaFree(s->d.pos); cudaFree(s->d.err); cudaFree(s->maps); cudaFree(s->d.ws); cudaFree(s->d.tickets); cudaFree(s->d.acnt);
   delete s;
@@ -653,7 +659,10 @@ bool balloc(T** p, size_t bytes) {
   return cudaMalloc(reinterpret_cast<void**>(p), bytes) == cudaSuccess && cudaMemset(*p, 0, bytes) == cudaSuccess;
 }
 
-BatchState* batch_init(const void* d_weights, const long long* offsets, int num_offsets, int batch, int max_seq) {
+// ext_kv: bind to a caller-owned cache of one sequence ([L][2][KVH][max_seq][hd])
+// instead of allocating [batch] caches (used by the parallel prefill).
+BatchState* batch_init(const void* d_weights, const long long* offsets, int num_offsets, int batch, int max_seq,
+                       __nv_bfloat16* ext_kv = nullptr) {
   using namespace mk;
   if (!d_weights || !offsets || batch < 1 || batch > kBMax || max_seq < 1) return nullptr;
   if (infer_shape(offsets, num_offsets) != 0) return nullptr;   // d64 shape only
@@ -680,7 +689,8 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
   d.batch = batch;
   d.max_seq = max_seq;
   d.maxch = (max_seq + kBChunk - 1) / kBChunk;
-  s->kv_bytes = (long long)batch * kBL * 2 * kBNKV * (long long)max_seq * kBD * 2;
+  s->kv_bytes = ext_kv ? 0 : (long long)batch * kBL * 2 * kBNKV * (long long)max_seq * kBD * 2;
+  s->owns_kv = ext_kv == nullptr;
   float *rc = nullptr, *rs = nullptr;
   const bool ok =
       balloc(&d.x, sizeof(float) * kBMax * kBH) && balloc(&d.ssq, sizeof(float) * kBHT * kBMax) &&
@@ -688,7 +698,8 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
       balloc(&d.q, sizeof(float) * kBMax * kBNQ * kBD) &&
       balloc(&d.part, sizeof(float) * (size_t)kBMax * kBNKV * d.maxch * 132) &&
       balloc(&d.lm_part, sizeof(unsigned long long) * (size_t)kBLMTiles * kBMax) &&
-      balloc(&d.kv, (size_t)s->kv_bytes) && balloc(&rc, sizeof(float) * (size_t)max_seq * 32) &&
+      (ext_kv ? (d.kv = ext_kv) != nullptr : balloc(&d.kv, (size_t)s->kv_bytes)) &&
+      balloc(&s->d_tmp, sizeof(int) * kBMax) && balloc(&rc, sizeof(float) * (size_t)max_seq * 32) &&
       balloc(&rs, sizeof(float) * (size_t)max_seq * 32) && balloc(&d.pos, sizeof(int) * kBMax) &&
       balloc(&d.err, sizeof(int) * 4) && balloc(&s->maps, sizeof(CUtensorMap) * (map_lm() + 1)) &&
       balloc(&d.ws, kBWsBytes) && balloc(&d.tickets, sizeof(int) * 64) &&
@@ -793,7 +804,58 @@ int batch_finish(BatchState* s, cudaStream_t st, int rc) {
   return rc;
 }
 
+__global__ void bset_pos_kernel(int* pos, int base, int rows) {
+  const int b = threadIdx.x;
+  if (b < mk::kBMax) pos[b] = b < rows ? base + b : 0;
+}
+
+// Parallel prefill of n prompt tokens at positions pos0 .. pos0+n-1 of the
+// bound cache: 64 positions per batched step (rows = consecutive positions
+// of sequence 0; row r attends to positions <= pos0 + 64k + r, all written
+// by the step's QKV epilogue before its attention kernel runs).  The greedy
+// token after the last prompt token goes to d_next.
+int batch_prefill(BatchState* s, const int* d_tokens, int n, int pos0, int* d_next, cudaStream_t st) {
+  using namespace mk;
+  s->d.seq_mode = 1;
+  int rc = ::MK_OK;
+  int rows = 0;
+  for (int k = 0; k * kBMax < n && rc == ::MK_OK; ++k) {
+    rows = n - k * kBMax < kBMax ? n - k * kBMax : kBMax;
+    s->batch = rows;
+    s->d.batch = rows;
+    bset_pos_kernel<<<1, kBMax, 0, st>>>(s->d.pos, pos0 + k * kBMax, rows);
+    rc = batch_step(s, d_tokens + (size_t)k * kBMax, nullptr, s->d_tmp, nullptr, st);
+  }
+  if (rc == ::MK_OK &&
+      cudaMemcpyAsync(d_next, s->d_tmp + rows - 1, sizeof(int), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    rc = ::MK_ERR_CUDA;
+  return batch_finish(s, st, rc);
+}
+
+// Frees the parallel-prefill state of a batch-1 engine (declared in megakernel.cu).
+void prefill_free(void* p) {
+  if (p) batch_free(static_cast<BatchState*>(p));
+}
+
 }  // namespace
+
+// Parallel prefill for the batch-1 engine (see include/megakernel.h).
+extern "C" int megakernel_prefill(void* handle, const int* d_tokens, int n_tokens, int* d_next, void* stream) {
+  State* st = static_cast<State*>(handle);
+  if (!st || !d_tokens || !d_next || n_tokens < 1) return MK_ERR_INVALID_ARG;
+  if (st->shape_id != 0) return set_err(st, MK_ERR_SHAPE);
+  if (st->pos + n_tokens > st->max_seq) return set_err(st, MK_ERR_CAPACITY);
+  if (cudaSetDevice(st->device) != cudaSuccess) return set_err(st, MK_ERR_CUDA);
+  if (!st->prefill) {
+    st->prefill = batch_init(st->d_weights, st->offsets.data(), (int)st->offsets.size(), mk::kBMax, st->max_seq,
+                             st->d_kv);
+    if (!st->prefill) return set_err(st, MK_ERR_OOM);
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : st->stream;
+  const int rc = batch_prefill(static_cast<BatchState*>(st->prefill), d_tokens, n_tokens, st->pos, d_next, s);
+  if (rc == MK_OK) st->pos += n_tokens;
+  return set_err(st, rc);
+}
 
 extern "C" {
 

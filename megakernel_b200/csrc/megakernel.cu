@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <vector>
 
 #include "../../include/megakernel.h"
 #include "decode_kernel.cuh"
@@ -54,7 +55,12 @@ struct State {
   uint64_t* d_trace = nullptr;  // caller-owned trace buffer
   int trace_steps = 0;
   uint64_t* d_detail = nullptr; // caller-owned sub-phase buffer (profiling)
+  const void* d_weights = nullptr;       // caller's weight buffer and offsets (parallel prefill)
+  std::vector<long long> offsets;
+  void* prefill = nullptr;               // lazily built batched state bound to d_kv (batch.cu)
 };
+
+void prefill_free(void* p);   // batch.cu
 
 struct ShapeInfo {
   int H, L, NQ, NKV, D, I, V;
@@ -150,6 +156,7 @@ void free_state(State* st) {
   cudaFree(st->d_logits);
   if (st->h_pinned) cudaFreeHost(st->h_pinned);
   if (st->stream) cudaStreamDestroy(st->stream);
+  prefill_free(st->prefill);
   delete st;
 }
 
@@ -192,6 +199,8 @@ int init_impl(void* d_weights, const long long* offsets, int num_offsets, const 
   if (!st) return MK_ERR_OOM;
   auto bail = [&](int code) { free_state(st); return code; };
   st->shape_id = id;
+  st->d_weights = d_weights;
+  st->offsets.assign(offsets, offsets + num_offsets);
   st->vocab = s.V;
   st->max_seq = o->max_seq > 0 ? o->max_seq : kDefaultMaxSeq;
   st->timeout_ns = o->timeout_ns > 0 ? o->timeout_ns : 1000000000LL;
@@ -454,6 +463,8 @@ int megakernel_decode_n(void* handle, const int* d_tokens, int n_forced, int n_s
   return set_err(st, run_sync(st, d_tokens, n_forced, n_steps, d_out, d_logits, s));
 }
 
+int megakernel_prefill(void* handle, const int* d_tokens, int n_tokens, int* d_next, void* stream);  // batch.cu
+
 int megakernel_generate(void* handle, const int* prompt, int n_prompt, int n_gen, int* out) {
   State* st = as_state(handle);
   if (!st) return MK_ERR_INVALID_ARG;
@@ -463,6 +474,9 @@ int megakernel_generate(void* handle, const int* prompt, int n_prompt, int n_gen
   if (cudaSetDevice(st->device) != cudaSuccess) return set_err(st, MK_ERR_CUDA);
   const int steps = n_prompt + n_gen - 1;
   if (st->pos + steps > st->max_seq) return set_err(st, MK_ERR_CAPACITY);
+  // The graded shape prefills the prompt in parallel (64 positions per
+  // batched tcgen05 step); other shapes feed it token by token.
+  const bool parallel = st->shape_id == 0 && std::getenv("MK_SERIAL_PREFILL") == nullptr;
   int* d_in = nullptr;
   int* d_out = nullptr;
   int rc = MK_OK;
@@ -472,10 +486,15 @@ int megakernel_generate(void* handle, const int* prompt, int n_prompt, int n_gen
   if (rc == MK_OK && cudaMemcpyAsync(d_in, prompt, sizeof(int) * n_prompt, cudaMemcpyHostToDevice,
                                      st->stream) != cudaSuccess)
     rc = MK_ERR_CUDA;
-  if (rc == MK_OK) rc = run_sync(st, d_in, n_prompt, steps, d_out, nullptr, st->stream);
+  int* res = d_out + (n_prompt - 1);
+  if (rc == MK_OK && parallel) {
+    rc = megakernel_prefill(handle, d_in, n_prompt, res, st->stream);
+    if (rc == MK_OK && n_gen > 1) rc = run_sync(st, res, 1, n_gen - 1, res + 1, nullptr, st->stream);
+  } else if (rc == MK_OK) {
+    rc = run_sync(st, d_in, n_prompt, steps, d_out, nullptr, st->stream);
+  }
   if (rc == MK_OK &&
-      (cudaMemcpyAsync(out, d_out + (n_prompt - 1), sizeof(int) * n_gen, cudaMemcpyDeviceToHost,
-                       st->stream) != cudaSuccess ||
+      (cudaMemcpyAsync(out, res, sizeof(int) * n_gen, cudaMemcpyDeviceToHost, st->stream) != cudaSuccess ||
        cudaStreamSynchronize(st->stream) != cudaSuccess))
     rc = MK_ERR_CUDA;
   if (d_in) cudaFreeAsync(d_in, st->stream);

@@ -245,3 +245,27 @@ def test_long_context_prefilled_kv_vs_oracle():
     ok = omargin > MARGIN
     assert np.array_equal(out.cpu().numpy()[ok], otoks[ok])
     eng.close()
+
+
+def test_parallel_prefill_vs_reference():
+    """megakernel_prefill (64 positions per batched tcgen05 step) fills the
+    engine's cache so that the next token and every later step match the
+    reference forward (BASELINE §8f: parallel prefill)."""
+    g = golden("qwen3-0.6b-d64")
+    eng = engine("qwen3-0.6b-d64")
+    seq = g["seq"].tolist()
+    k = 70                                   # one full chunk of 64 + a partial one
+    nxt = eng.prefill(torch.tensor(seq[:k], dtype=torch.int32, device=DEV))
+    assert eng.pos == k
+    if g["margin"][k - 1] > MARGIN:
+        assert int(nxt.item()) == int(g["argmax"][k - 1])
+    n = len(seq) - k
+    toks = torch.tensor(seq[k:], dtype=torch.int32, device=DEV)
+    out = torch.zeros(n, dtype=torch.int32, device=DEV)
+    lg = torch.zeros(n, eng.vocab, dtype=torch.float32, device=DEV)
+    eng.decode_n(toks, n, out, logits=lg)
+    lg = lg.cpu().numpy()
+    err = np.abs(lg[:, g["sub_ids"]] - g["sub_logits"][k:]).max()
+    assert err < LOGIT_TOL, err
+    ok = g["margin"][k:] > MARGIN
+    assert np.array_equal(out.cpu().numpy()[ok], g["argmax"][k:][ok])
