@@ -297,6 +297,11 @@ struct AttnWarpSmem {
 };
 constexpr size_t kBAttnSmem = sizeof(AttnWarpSmem) * kBAttnWarps;
 
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -524,21 +529,20 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       __stcg(o + hh * 66 + 64, mx);
       __stcg(o + hh * 66 + 65, ls);
     }
-    // Ticket: the warp finishing the last chunk of (b, h) merges.
-    __threadfence();
+    // Ticket: the warp finishing the last chunk of (b, h) merges.  The
+    // acq_rel atomic releases this warp's partial stores (ordered before it
+    // by __syncwarp; release is cumulative) and, for the last warp, acquires
+    // every other chunk's.
     __syncwarp();
     int last = 0;
     if (lane == 0) {
       const int nc = p / kBChunk + 1;
-      const int old = atomicAdd(d.acnt + b * kBNKV + h, 1);
+      const int old = atom_add_acq_rel(d.acnt + b * kBNKV + h, 1);
       last = old == nc - 1;
       if (last) d.acnt[b * kBNKV + h] = 0;
     }
     last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) {
-      __threadfence();
-      attn_merge(d, b, h, lane);
-    }
+    if (last) attn_merge(d, b, h, lane);
   }
 }
 

@@ -8,7 +8,7 @@
 //
 // Per CTA (persistent over 64-column output tiles, 256 threads):
 //   warp 0      TMA producer: A block (64 K x 128 rows, SW128) and two 32-row
-//               W blocks per stage into a 4-stage ring (full/empty mbarriers);
+//               W blocks per stage into an 8-stage ring (full/empty mbarriers);
 //   warp 1      TMEM owner and MMA issuer: 4 x tcgen05.mma (K=16 each) per
 //               stage into one of two 64-column fp32 accumulators, commits to
 //               the stage's empty barrier and, per tile, to tmem_full;
@@ -32,7 +32,7 @@
 
 namespace mk {
 
-constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 4;
+constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 8;
 constexpr int kTcABytes = kTcBM * kTcBK * 2;          // 16 KB
 constexpr int kTcWBytes = kTcBN * kTcBK * 2;          //  8 KB
 constexpr int kTcStageBytes = kTcABytes + kTcWBytes;  // 24 KB
