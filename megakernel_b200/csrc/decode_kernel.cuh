@@ -381,6 +381,10 @@ __device__ __forceinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t*
 
 }  // namespace mk
 
+#ifndef MK_MERGE_ML_FIRST
+#define MK_MERGE_ML_FIRST 1
+#endif
+
 namespace mk {
 
 // Resolve up to NB tagged words already loaded into w[]: while any of them
@@ -866,6 +870,7 @@ __device__ MK_PHASE void attend_block(Smem<S>& sm, const __nv_bfloat16* K1, cons
     const int part = tid / GD, g = (tid / D) % GRP, d = tid % D;
     float a0 = 0.f, a1 = 0.f;
     int pos = part;
+#pragma unroll 4
     for (; pos + PARTS < n1; pos += 2 * PARTS) {
       a0 = fmaf(sm.sc[g][pos], __bfloat162float(V1[(size_t)pos * D + d]), a0);
       a1 = fmaf(sm.sc[g][pos + PARTS], __bfloat162float(V1[(size_t)(pos + PARTS) * D + d]), a1);
@@ -1005,11 +1010,14 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
     const uint32_t sv = (kc + 1) % nst, pv = ((kc + 1) / nst) & 1u;
     const bool okk = wait_bar(P, sm, &sm.full[sk], pk);
     const bool okv = okk && wait_bar(P, sm, &sm.full[sv], pv);
+    const int blk = (a - c0) / S::SUBP;
+    if (blk < 4) MK_DP(20 + 2 * blk);
     if (!consumer_any(kConsumerThreads, !(okk && okv))) {
       attend_block(sm, reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sk * S::STB),
                    reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sv * S::STB), n,
                    &sm.kx[s0][0], &sm.vx[s0][0], ne, acc);
     }
+    if (blk < 4) MK_DP(21 + 2 * blk);
     ne = 0;
     if (lane == 0) { mbar_arrive(&sm.empty[sk]); mbar_arrive(&sm.empty[sv]); }
     kc += 2;
@@ -1034,14 +1042,13 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
   }
   MK_DP(6);
   if (last && tid < D) {
-    // Append the current K/V (bf16) at position p -- after the partial is
-    // published, so the fences stay off this step's critical path; the first
-    // reader of position p is the next step.
+    // Append the current K/V (bf16) at position p, after the partial is
+    // published.  Its first reader is the next step, so the fences that make
+    // it visible (to other CTAs' loads and TMA copies) are issued once per
+    // step, before this CTA publishes its LM-head pair (fence_kv_appends).
     const int d = tid;
     P.kv[kv_index<S>(l, 0, h, p, P.max_seq) + d] = sm.kx[1][d];
     P.kv[kv_index<S>(l, 1, h, p, P.max_seq) + d] = sm.vx[1][d];
-    fence_proxy_async_global();
-    __threadfence();
   }
   consumer_sync(kConsumerThreads);
   return kc - kc0;
@@ -1074,32 +1081,61 @@ __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, u
   const int e0 = threadIdx.x * EPT;
   const bool active = e0 < S::Q;
   const int qh = active ? e0 / D : 0, d0 = e0 % D, g = qh % GRP;
-  const uint64_t* b = att + ((size_t)(qh / GRP) * nc * GRP + g) * (D + 2);
-  // Accumulator words: all chunks' EPT words loaded up front (nc <= 8).
-  uint64_t w[kMaxChunksPerHead * EPT];
-  const uint64_t* sp[kMaxChunksPerHead * EPT];
-#pragma unroll
-  for (int j = 0; j < kMaxChunksPerHead; ++j)
-#pragma unroll
-    for (int k = 0; k < EPT; ++k) {
-      sp[j * EPT + k] = b + (size_t)j * stride + d0 + k;
-      w[j * EPT + k] = (active && j < nc) ? ld_relaxed(sp[j * EPT + k]) : 0;
-    }
-  if (active) resolve_tagged<S, kMaxChunksPerHead * EPT>(P, sm, w, sp, nc * EPT, ta);
+  const uint64_t* b = att + ((size_t)(qh / GRP) * nc * GRP + g) * (D + 2) + d0;
+  // Accumulator words, kGroup chunks at a time (registers bound the group):
+  // the first group's loads are issued before the (m, l) sync, so with
+  // nc <= kGroup the merge costs one polling round trip.  Word q of a group
+  // is chunk j0 + q / EPT, element q % EPT.
+  constexpr int kGroup = 8, NW = kGroup * EPT;
+  uint64_t w[NW];
+#if MK_MERGE_ML_FIRST
+  // Poll the accumulator words only once every (m, l) pair is present: their
+  // writers publish them together, so one round then finds nearly all of
+  // them, instead of every thread of every CTA re-polling its words while
+  // the items are still running (which also slows the writers' stores).
   consumer_sync(kConsumerThreads);
+#pragma unroll
+  for (int q = 0; q < NW; ++q)
+    w[q] = (active && q / EPT < nc) ? ld_relaxed(b + (size_t)(q / EPT) * stride + q % EPT) : 0;
+#else
+#pragma unroll
+  for (int q = 0; q < NW; ++q)
+    w[q] = (active && q / EPT < nc) ? ld_relaxed(b + (size_t)(q / EPT) * stride + q % EPT) : 0;
+  consumer_sync(kConsumerThreads);
+#endif
+  float M = -INFINITY, den = 0.f, acc[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) acc[k] = 0.f;
   if (active) {
-    float M = -INFINITY;
     for (int j = 0; j < nc; ++j) M = fmaxf(M, sm.mlbuf[2 * (qh * nc + j)]);
-    float den = 0.f, acc[EPT];
+    for (int j0 = 0; j0 < nc; j0 += kGroup) {
+      const int nvw = min(kGroup, nc - j0) * EPT;
+      const uint64_t* bg = b + (size_t)j0 * stride;
+      if (j0 > 0) {
 #pragma unroll
-    for (int k = 0; k < EPT; ++k) acc[k] = 0.f;
+        for (int q = 0; q < NW; ++q) w[q] = q < nvw ? ld_relaxed(bg + (size_t)(q / EPT) * stride + q % EPT) : 0;
+      }
+      bool miss = false;
 #pragma unroll
-    for (int j = 0; j < kMaxChunksPerHead; ++j) {
-      if (j < nc) {
-        const float cj = expf(sm.mlbuf[2 * (qh * nc + j)] - M);
-        den = fmaf(sm.mlbuf[2 * (qh * nc + j) + 1], cj, den);
+      for (int q = 0; q < NW; ++q) miss |= q < nvw && (uint32_t)(w[q] >> 32) != ta;
+      Spin spn;
+      while (miss && spn.keep_going(P, sm)) {
+        __nanosleep(200);
+        miss = false;
 #pragma unroll
-        for (int k = 0; k < EPT; ++k) acc[k] = fmaf(__uint_as_float((uint32_t)w[j * EPT + k]), cj, acc[k]);
+        for (int q = 0; q < NW; ++q)
+          if (q < nvw && (uint32_t)(w[q] >> 32) != ta) w[q] = ld_relaxed(bg + (size_t)(q / EPT) * stride + q % EPT);
+#pragma unroll
+        for (int q = 0; q < NW; ++q) miss |= q < nvw && (uint32_t)(w[q] >> 32) != ta;
+      }
+#pragma unroll
+      for (int j = 0; j < kGroup; ++j) {
+        if (j * EPT < nvw) {
+          const float cj = expf(sm.mlbuf[2 * (qh * nc + j0 + j)] - M);
+          den = fmaf(sm.mlbuf[2 * (qh * nc + j0 + j) + 1], cj, den);
+#pragma unroll
+          for (int k = 0; k < EPT; ++k) acc[k] = fmaf(__uint_as_float((uint32_t)w[j * EPT + k]), cj, acc[k]);
+        }
       }
     }
     const float inv = 1.f / den;
@@ -1123,6 +1159,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
     const int nc = chunks_per_head<S>(p);
     const int nitems = S::NKV * nc;
     const long long clk0 = clock64();
+    bool appended = false;
     {
       const __nv_bfloat16* er = sm.wtab[0] + (size_t)tok * S::H;
       for (int i = tid; i < S::H; i += kConsumerThreads) sm.xres[i] = __bfloat162float(er[i]);
@@ -1181,8 +1218,10 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
       {
         int ilo, ihi;
         items_of_cta(cta, l, nitems, N, ilo, ihi);
-        for (int i = ilo; i < ihi; ++i)
+        for (int i = ilo; i < ihi; ++i) {
           kc += attention_item<S>(P, sm, ring, kc, t, l, p, seq, i / nc, i % nc, nc, i);
+          appended |= (i % nc == nc - 1);
+        }
       }
       // ---- P3: merge -> O projection + residual --------------------------------
       {
@@ -1254,6 +1293,14 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
       }
     }
     // ---- final RMSNorm -> LM head -> argmax ------------------------------------
+    // K/V appended during this step become visible before this CTA's LM-head
+    // pair is published: every reader of them (next step's attention, the
+    // copy engines two steps on) first observes all CTAs' pairs of this step.
+    if (appended && tid < S::D) {
+      fence_proxy_async_global();
+      __threadfence();
+    }
+    appended = false;
     GainRegs<S> fgains;
     fgains.load(sm.wtab[1]);
     wait_tagged(P, sm, P.hop + HopLayout<S>::X + (size_t)(S::L & 1) * S::H, S::H,

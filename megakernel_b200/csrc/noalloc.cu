@@ -39,7 +39,7 @@ constexpr size_t kWtabOff = kErrOff + 256;                              // NOFF 
 constexpr size_t kCosOff = kWtabOff + ((SNA::NOFF * 8 + 255) / 256) * 256;
 constexpr size_t kRopeBytes = (size_t)kMaxPos * (SNA::D / 2) * sizeof(float);
 constexpr size_t kSinOff = kCosOff + kRopeBytes;
-constexpr size_t kScratchBytes = kSinOff + kRopeBytes;                  // ~0.76 MB
+constexpr size_t kScratchBytes = kSinOff + kRopeBytes;                  // ~0.87 MB
 static_assert(kScratchBytes == MK_NOALLOC_SCRATCH_BYTES, "header and layout agree");
 
 // The only scratch this entry point uses.  In host code `g_scratch` is a

@@ -24,7 +24,13 @@ constexpr int kRingBytes = 176 * 1024;
 constexpr int kMaxCtas = 256;
 constexpr int kRowsMax = 256;           // weight rows one CTA owns in one phase
 constexpr int kRowPad = 16;             // bytes between weight rows in a ring stage
-constexpr int kMaxChunksPerHead = 8;    // attention split-KV chunks per KV head
+constexpr int kMaxChunksPerHead = 16;   // attention split-KV chunks per KV head
+// Fewest cached positions per chunk: below this a chunk's fixed costs (q/k/v
+// wait, QK-norm, RoPE, partial publish) outweigh the positions it walks.
+#ifndef MK_CHUNK_MIN_POS
+#define MK_CHUNK_MIN_POS 128
+#endif
+constexpr int kChunkMinPos = MK_CHUNK_MIN_POS;
 
 template <int H_, int L_, int NQ_, int NKV_, int D_, int I_, int V_, int STB_>
 struct ShapeT {
@@ -33,7 +39,6 @@ struct ShapeT {
   static constexpr int STB = STB_;                          // ring stage bytes
   static constexpr int NST = kRingBytes / STB;              // ring stages
   static constexpr int SUBP = STB / (D * 2);                // KV positions per stage
-  static constexpr int CPOS = 2 * SUBP;                     // target positions per chunk
   static constexpr int XIN = (H > Q ? (H > I ? H : I) : (Q > I ? Q : I));
   static constexpr int NOFF = 2 + 11 * L;
   // Weight rows sit in a stage at a pitch of 2K + 16 bytes, so the 8 rows an
@@ -70,10 +75,12 @@ __host__ __device__ inline int phase_rot(int layer, int phase, int N) {
   return (int)((unsigned)((layer * 5 + phase) * 37) % (unsigned)N);
 }
 
-// Attention split-KV plan for a step at position p (p cached positions).
+// Attention split-KV plan for a step at position p (p cached positions): one
+// chunk per kChunkMinPos positions (rounded up), at most kMaxChunksPerHead,
+// so up to NKV * 16 = 128 CTAs walk the cache at once.
 template <class S>
 __host__ __device__ inline int chunks_per_head(int p) {
-  int nc = (p + S::CPOS - 1) / S::CPOS;
+  int nc = (p + kChunkMinPos - 1) / kChunkMinPos;
   if (nc < 1) nc = 1;
   if (nc > kMaxChunksPerHead) nc = kMaxChunksPerHead;
   return nc;
