@@ -250,12 +250,54 @@ def run_ours(args, world, rank, local):
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
+    if world > 1 and not args.no_tp:
+        line["tensor_parallel"] = run_tp(args, world, rank, local, shape, flat, offs, prompt, check)
     if rank == 0 and world == 1 and not args.no_batched:
         line["long_context"] = run_long(shape, flat, offs, dev, peak)
         line["batched"] = run_batched(shape, flat, offs, dev, peak)
     if rank == 0:
         print(json.dumps(line), flush=True)
     eng.close()
+
+
+def run_tp(args, world, rank, local, shape, flat, offs, prompt, single_tokens):
+    """BASELINE.json configs[4](b): one batch-1 stream split over all ranks
+    (MLP and LM-head rows per rank, partial sums and argmax pairs exchanged
+    over NVLink inside the kernel); same prompt and 512 greedy tokens as the
+    replica line.  Reported beside the replica (weak-scaling) headline."""
+    from megakernel_b200 import tp
+    dev = torch.device("cuda", local)
+    eng = tp.make_engine(flat, offs, shape, device=local, max_seq=PROMPT + GEN + 8)
+    first = eng.prefill(torch.tensor(prompt, dtype=torch.int32, device=dev))
+    out = torch.zeros(GEN, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        eng.set_pos(PROMPT)
+        eng.decode_n(first, 1, out, n_steps=GEN, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    for s, e in ev:
+        s.record(stream)
+        step()
+        e.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev), world, dev) / args.steps
+    got = out.cpu().tolist()
+    same = sum(1 for a, b in zip(got, single_tokens) if a == b)
+    eng.close()
+    wb = shape.tp_weight_bytes(world)
+    return {"workload": f"configs[4](b): tensor parallel over {world} GPUs, B=1, {PROMPT}-token prompt, "
+                        f"{GEN} greedy tokens (MLP + LM-head rows split, NVLink exchange in-kernel)",
+            "value": GEN / (ms / 1e3), "unit": "tok/s", "us_per_token": ms * 1e3 / GEN,
+            "weight_bytes_per_gpu": wb, "gpu_launches": args.steps,
+            "greedy_tokens_equal_to_single_gpu": f"{same}/{GEN}"}
 
 
 def run_long(shape, flat, offs, dev, peak):
@@ -337,6 +379,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-tokens", type=int, default=12)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="skip the configs[4](b) tensor-parallel line (N > 1)")
     ap.add_argument("--no-batched", action="store_true",
                     help="skip the configs[2] long-context and configs[3] batched lines")
     args = ap.parse_args()

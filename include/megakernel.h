@@ -74,7 +74,8 @@ int megakernel_init_ex(void* d_weights, const long long* offsets, int num_offset
 /* Run n_steps decode steps in ONE kernel launch.  Step s feeds d_tokens[s] for
  * s < n_forced (teacher forcing / prefill) and the previous step's argmax
  * afterwards.  d_out[s] receives the argmax of step s.  d_logits, if not NULL,
- * receives [n_steps, vocab] fp32 logits.  stream: cudaStream_t or NULL.
+ * receives [n_steps, vocab] fp32 logits.  stream: cudaStream_t, or NULL for the
+ * default stream.
  * Blocks until the launch finishes; the position advances by n_steps. */
 int megakernel_decode_n(void* handle, const int* d_tokens, int n_forced, int n_steps,
                         int* d_out, float* d_logits, void* stream);
@@ -184,6 +185,27 @@ int megakernel_batch_get_pos(void* handle, int* h_pos);
 void* megakernel_batch_kv_ptr(void* handle);
 long long megakernel_batch_kv_bytes(void* handle);
 int megakernel_batch_last_error(void* handle);
+
+/* ---- tensor parallelism over NVLink (no reference counterpart) ------------
+ * configs[4](b): one process per GPU, tp_size in {2, 4, 8} (graded d64
+ * shape; the tiny test shape also at 2).  Each rank reads its slice of the
+ * MLP (gate/up rows and down columns [rank I/tp, (rank+1) I/tp)) and of the
+ * LM head (vocab rows [rank V/tp, (rank+1) V/tp)); attention, QKV and O stay
+ * replicated.  Inside the kernel each rank stores its partial down projection
+ * (1024 fp32 per layer) and its per-CTA (max, index) pairs straight into
+ * every rank's exchange buffer over NVLink; every rank sums the partials in
+ * rank order, so all ranks hold identical activations and pick the same
+ * token.  Set-up: megakernel_tp_init on every rank, exchange the 64-byte
+ * handles of megakernel_tp_ipc_handle (rank order), then
+ * megakernel_tp_connect.  After that every decode call of this ABI
+ * (megakernel_decode, _decode_n, _generate, _prefill, _set_pos, _reset) works
+ * in TP mode, and all ranks must make the same calls with the same arguments.
+ * Captured logits hold only this rank's vocab rows. */
+int megakernel_tp_init(void* d_weights, const long long* offsets, int num_offsets,
+                       const mk_options* opts, int tp_rank, int tp_size, void** out_handle);
+int megakernel_tp_ipc_handle(void* handle, void* out_64_bytes);
+int megakernel_tp_connect(void* handle, const void* handles_tp_size_x_64_bytes);
+int megakernel_tp_info(void* handle, int* rank, int* size);
 
 /* ---- host-only helpers (no GPU needed) ----------------------------------- */
 

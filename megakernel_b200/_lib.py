@@ -16,10 +16,13 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libmegakernel.so")
 HEADER = os.path.join(ROOT, "include", "megakernel.h")
 SOURCES = [os.path.join(CSRC, f) for f in ("megakernel.cu", "noalloc.cu", "decode_kernel.cuh", "ptx.cuh",
-                                                  "shapes.cuh", "batch.cu", "tc_gemm.cuh", "tc_ptx.cuh")]
+                                                  "shapes.cuh", "batch.cu", "tc_gemm.cuh", "tc_ptx.cuh",
+                                                  "tp.cu")]
+# Translation units, compiled in parallel and linked into one library.
+UNITS = ["megakernel.cu", "tp.cu"]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
-              "-shared", "-Xcompiler", "-fPIC"]
+              "-Xcompiler", "-fPIC"]
 
 MK_OK = 0
 ERRORS = {0: "ok", -1: "invalid argument", -2: "CUDA runtime error", -3: "in-kernel wait timed out",
@@ -38,14 +41,28 @@ def build(force: bool = False, verbose: bool = False) -> str:
         lib_m = os.path.getmtime(LIB_PATH)
         if all(os.path.getmtime(s) <= lib_m for s in SOURCES + [HEADER]):
             return LIB_PATH
-    cmd = [nvcc()] + NVCC_FLAGS + [os.path.join(CSRC, "megakernel.cu"), "-o", LIB_PATH + ".tmp"]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    objs, procs = [], []
+    for u in UNITS:
+        obj = os.path.join(PKG_DIR, u.replace(".cu", ".o"))
+        cmd = [nvcc()] + NVCC_FLAGS + (["-Xptxas=-v"] if verbose else []) + \
+            ["-c", os.path.join(CSRC, u), "-o", obj]
+        objs.append(obj)
+        procs.append(subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True))
+    errs = []
+    for p in procs:
+        _, err = p.communicate()
+        if p.returncode != 0:
+            errs.append(err)
+        elif verbose:
+            print(err)
+    if errs:
+        raise RuntimeError("nvcc failed:\n" + "\n".join(errs))
+    r = subprocess.run([nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared"] + objs +
+                       ["-o", LIB_PATH + ".tmp"], capture_output=True, text=True)
+    for o in objs:
+        os.remove(o)
     if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed:\n{r.stderr}")
-    if verbose:
-        print(r.stderr)
+        raise RuntimeError(f"nvcc link failed:\n{r.stderr}")
     os.replace(LIB_PATH + ".tmp", LIB_PATH)
     return LIB_PATH
 
@@ -102,6 +119,11 @@ def signatures() -> dict:
         "megakernel_batch_kv_ptr": ([vp], vp),
         "megakernel_batch_kv_bytes": ([vp], c_ll),
         "megakernel_batch_last_error": ([vp], c_int),
+        "megakernel_tp_init": ([vp, llp, c_int, ctypes.POINTER(MkOptions), c_int, c_int, ctypes.POINTER(vp)],
+                               c_int),
+        "megakernel_tp_ipc_handle": ([vp, vp], c_int),
+        "megakernel_tp_connect": ([vp, vp], c_int),
+        "megakernel_tp_info": ([vp, ip, ip], c_int),
         "megakernel_infer_shape": ([llp, c_int], c_int),
         "megakernel_rope_table": ([c_int, ctypes.c_double, c_int, fp, fp], c_int),
         "megakernel_plan_bytes": ([c_int, c_int, c_int, llp], c_int),

@@ -31,7 +31,7 @@ class MegakernelEngine:
 
     def __init__(self, weights_path=None, offsets_path=None, lib_path=None, tokenizer=None, *,
                  flat=None, offsets=None, shape=None, device=0, max_seq=0, num_ctas=0,
-                 timeout_ns=0, debug_skip_cta=-1):
+                 timeout_ns=0, debug_skip_cta=-1, tp_rank=0, tp_size=1):
         self.tokenizer = tokenizer
         self.lib = _lib.load(lib_path)
         self._handle = None
@@ -58,10 +58,19 @@ class MegakernelEngine:
         opts.timeout_ns = timeout_ns
         opts.debug_skip_cta = debug_skip_cta
         h = ctypes.c_void_p()
-        rc = self.lib.megakernel_init_ex(ctypes.c_void_p(self._gpu_buffer.data_ptr()),
-                                         self._offsets_arr, self._num_offsets,
-                                         ctypes.byref(opts), ctypes.byref(h))
-        _lib.check(rc, "megakernel_init_ex")
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        if tp_size > 1:
+            # Tensor-parallel rank: call tp_connect (megakernel_b200.tp.connect)
+            # on every rank before decoding.
+            rc = self.lib.megakernel_tp_init(ctypes.c_void_p(self._gpu_buffer.data_ptr()),
+                                             self._offsets_arr, self._num_offsets, ctypes.byref(opts),
+                                             int(tp_rank), int(tp_size), ctypes.byref(h))
+            _lib.check(rc, "megakernel_tp_init")
+        else:
+            rc = self.lib.megakernel_init_ex(ctypes.c_void_p(self._gpu_buffer.data_ptr()),
+                                             self._offsets_arr, self._num_offsets,
+                                             ctypes.byref(opts), ctypes.byref(h))
+            _lib.check(rc, "megakernel_init_ex")
         self._handle = h.value
         self.vocab = self.shape.vocab
         self.max_seq = self.lib.megakernel_max_seq(self._handle)
@@ -195,7 +204,9 @@ class MegakernelEngine:
         assert tokens.dtype == torch.int32 and out.dtype == torch.int32 and out.numel() >= n_steps
         assert tokens.is_contiguous() and out.is_contiguous()
         lp = logits.data_ptr() if logits is not None else None
-        st = stream.cuda_stream if stream is not None else None
+        # Default: torch's current stream, so the launch is ordered after the
+        # work that produced `tokens` and initialised the output tensors.
+        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
         rc = self.lib.megakernel_decode_n(self._handle, tokens.data_ptr(), int(n_forced), int(n_steps),
                                           out.data_ptr(), lp, st)
         _lib.check(rc, "megakernel_decode_n")
@@ -207,10 +218,24 @@ class MegakernelEngine:
         step; returns the greedy next token as a 1-element device tensor."""
         assert tokens.dtype == torch.int32 and tokens.is_contiguous()
         nxt = torch.empty(1, dtype=torch.int32, device=tokens.device)
-        st = stream.cuda_stream if stream is not None else None
+        # Default: torch's current stream, so the launch is ordered after the
+        # work that produced `tokens` and initialised the output tensors.
+        st = (stream or torch.cuda.current_stream(self.device)).cuda_stream
         rc = self.lib.megakernel_prefill(self._handle, tokens.data_ptr(), int(tokens.numel()), nxt.data_ptr(), st)
         _lib.check(rc, "megakernel_prefill")
         return nxt
+
+    def tp_ipc_handle(self) -> bytes:
+        """64-byte CUDA IPC handle of this rank's exchange buffer."""
+        buf = ctypes.create_string_buffer(64)
+        _lib.check(self.lib.megakernel_tp_ipc_handle(self._handle, buf), "megakernel_tp_ipc_handle")
+        return buf.raw
+
+    def tp_connect(self, handles):
+        """Map every rank's exchange buffer (handles in rank order)."""
+        assert len(handles) == self.tp_size and all(len(h) == 64 for h in handles)
+        buf = ctypes.create_string_buffer(b"".join(handles), 64 * self.tp_size)
+        _lib.check(self.lib.megakernel_tp_connect(self._handle, buf), "megakernel_tp_connect")
 
     def set_logits_capture(self, enable=True):
         _lib.check(self.lib.megakernel_set_logits_capture(self._handle, int(enable)))

@@ -855,7 +855,9 @@ extern "C" int megakernel_prefill(void* handle, const int* d_tokens, int n_token
                              st->d_kv);
     if (!st->prefill) return set_err(st, MK_ERR_OOM);
   }
-  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : st->stream;
+  // NULL: the default stream, as the reference's calls use, so the launch is
+  // ordered after the caller's earlier default-stream work on its buffers.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int rc = batch_prefill(static_cast<BatchState*>(st->prefill), d_tokens, n_tokens, st->pos, d_next, s);
   if (rc == MK_OK) st->pos += n_tokens;
   return set_err(st, rc);

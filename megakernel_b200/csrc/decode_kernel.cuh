@@ -69,19 +69,28 @@ struct KParams {
   uint64_t* trace;                // optional stamps [trace_steps][ncta][Trace::kPoints]
   int trace_steps;
   uint64_t* detail;               // optional [trace_steps][ncta][64] sub-phase stamps of layer 1
+  // Tensor-parallel launches (template TP > 1) only: this GPU's rank and the
+  // hop buffer of every rank (peer_hop[tp_rank] is this GPU's own), mapped
+  // into this process by CUDA IPC.
+  int tp_rank;
+  uint64_t* peer_hop[kMaxTP];
 };
 
-// Offsets (in 64-bit words) of the tagged activation buffers.
-template <class S>
+// Offsets (in 64-bit words) of the tagged activation buffers.  With tensor
+// parallelism over TP GPUs, X holds one slot per rank (each rank's partial
+// down projection, written by that rank over NVLink) and LM one (max, index)
+// pair per (rank, CTA); the other hops stay on the GPU.
+template <class S, int TP = 1>
 struct HopLayout {
   static constexpr int kAttWords = S::NKV * kMaxChunksPerHead * S::GRP * (S::D + 2);
-  static constexpr long long X = 0;                       // [2][H]  layer input
-  static constexpr long long QKV = X + 2 * S::H;           // [2][QKV]
+  // The GPU-local hops come first, so their offsets do not depend on TP.
+  static constexpr long long QKV = 0;                      // [2][QKV]
   static constexpr long long ATT = QKV + 2 * S::QKV;       // [2][items][GRP][D+2]
   static constexpr long long XA = ATT + 2LL * kAttWords;   // [2][H]  after attention
   static constexpr long long HM = XA + 2 * S::H;           // [2][I]  silu(g)*u
-  static constexpr long long LM = HM + 2 * S::I;           // [2][kMaxCtas][2]
-  static constexpr long long TOTAL = LM + 2 * kMaxCtas * 2;
+  static constexpr long long X = HM + 2 * S::I;            // [2][TP][H]  layer input
+  static constexpr long long LM = X + 2LL * TP * S::H;     // [2][TP * kMaxCtas][2]
+  static constexpr long long TOTAL = LM + 2LL * TP * kMaxCtas * 2;
 };
 
 // Tag of phase `k` (0 qkv, 1 att, 2 xa, 3 hm, 4 x-out) of layer `l` at step seq.
@@ -277,8 +286,11 @@ struct Producer {
       issue(base + (size_t)r * K, (uint32_t)(n * 2 * K));
     }
   }
-  // Rows for the tensor-core GEMV: one copy per row, at pitch 2K + 16.
-  __device__ __forceinline__ void rows_padded(const __nv_bfloat16* base, int r0, int r1, int K) {
+  // Rows for the tensor-core GEMV: one copy per row, at pitch 2K + 16.  Row
+  // r starts at base + r * stride (stride > K: a column slice of each row).
+  __device__ __forceinline__ void rows_padded(const __nv_bfloat16* base, int r0, int r1, int K,
+                                              int stride = 0) {
+    if (stride == 0) stride = K;
     const int pitch = 2 * K + kRowPad;
     const int rpc = S::STB / pitch;
     for (int r = r0; r < r1 && ok; r += rpc) {
@@ -287,7 +299,7 @@ struct Producer {
       if (!acquire(slot)) return;
       mbar_arrive_expect_tx(&sm->full[slot], (uint32_t)(n * 2 * K));
       for (int i = 0; i < n; ++i)
-        bulk_g2s(ring + (size_t)slot * S::STB + (size_t)i * pitch, base + (size_t)(r + i) * K,
+        bulk_g2s(ring + (size_t)slot * S::STB + (size_t)i * pitch, base + (size_t)(r + i) * stride,
                  (uint32_t)(2 * K), &sm->full[slot], pol);
       ++k;
     }
@@ -330,8 +342,12 @@ struct Producer {
   }
 };
 
-template <class S>
+template <class S, int TP>
 __device__ __forceinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ring, int cta) {
+  // With TP > 1 this GPU reads its rank's slice of the MLP (rows of gate/up,
+  // columns of down) and of the LM head (vocab rows); the rest is replicated.
+  constexpr int IR = S::I / TP, VR = S::V / TP;
+  const int rank = TP > 1 ? P.tp_rank : 0;
   if ((threadIdx.x & 31) != 0) return;
   const int N = P.ncta;
   // Its state lives in shared memory: the methods take `this`, and a stack
@@ -366,15 +382,15 @@ __device__ __forceinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t*
       pr.kv_items(t, l, p, nc, ilo, ihi);
       split_rows(S::H, N, cta, phase_rot(l, 1, N), r0, r1);
       pr.rows_padded(wptr(l, W_O), r0, r1, S::Q);
-      split_rows(S::I, N, cta, phase_rot(l, 2, N), r0, r1);
-      pr.rows_padded(wptr(l, W_GATE), r0, r1, S::H);
-      pr.rows_padded(wptr(l, W_UP), r0, r1, S::H);
+      split_rows(IR, N, cta, phase_rot(l, 2, N), r0, r1);
+      pr.rows_padded(wptr(l, W_GATE), rank * IR + r0, rank * IR + r1, S::H);
+      pr.rows_padded(wptr(l, W_UP), rank * IR + r0, rank * IR + r1, S::H);
       split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
-      pr.rows_padded(wptr(l, W_DOWN), r0, r1, S::I);
+      pr.rows_padded(wptr(l, W_DOWN) + (size_t)rank * IR, r0, r1, IR, S::I);
     }
     int r0, r1;
-    split_rows(S::V, N, cta, phase_rot(S::L, 4, N), r0, r1);
-    pr.rows(sm.wtab[0], r0, r1, S::H);
+    split_rows(VR, N, cta, phase_rot(S::L, 4, N), r0, r1);
+    pr.rows(sm.wtab[0], rank * VR + r0, rank * VR + r1, S::H);
   }
   if (!pr.ok) pr.drain();
 }
@@ -392,7 +408,7 @@ namespace mk {
 // polling costs one L2 round trip however many words a thread owns.
 // Bounded like every wait; on expiry the caller proceeds with stale values
 // (the abort flag is set and the step is abandoned at the next barrier).
-template <class S, int NB>
+template <class S, int NB, bool SYS = false>
 __device__ __forceinline__ void resolve_tagged(const KParams& P, Smem<S>& sm, uint64_t (&w)[NB],
                                                const uint64_t* (&src)[NB], int nvalid, uint32_t tag) {
   bool miss = false;
@@ -407,7 +423,7 @@ __device__ __forceinline__ void resolve_tagged(const KParams& P, Smem<S>& sm, ui
     __nanosleep(200);
 #pragma unroll
     for (int k = 0; k < NB; ++k)
-      if (k < nvalid && (uint32_t)(w[k] >> 32) != tag) w[k] = ld_relaxed(src[k]);
+      if (k < nvalid && (uint32_t)(w[k] >> 32) != tag) w[k] = SYS ? ld_relaxed_sys(src[k]) : ld_relaxed(src[k]);
     miss = false;
 #pragma unroll
     for (int k = 0; k < NB; ++k) miss |= (k < nvalid) && (uint32_t)(w[k] >> 32) != tag;
@@ -550,9 +566,12 @@ struct GemvPlan {
   static constexpr int PITCH = S::template pitch<K>();
   static constexpr int RPC = S::template rows_per_stage<K>();
   static constexpr int KS = K / 16;
-  static constexpr int ITER = KS / kConsumerWarps;
+  static constexpr int ITER = (KS + kConsumerWarps - 1) / kConsumerWarps;
   static constexpr int PIT = ITER < 2 ? ITER : 2;   // slices preloaded per tile
-  static_assert(RPC >= 1 && KS % kConsumerWarps == 0, "GEMV shape");
+  // Ragged K (a tensor-parallel column slice): the last slices exist for only
+  // some warps, which skip the rest (a warp-uniform test).
+  static constexpr bool kRag = KS % kConsumerWarps != 0;
+  static_assert(RPC >= 1 && K % 16 == 0, "GEMV shape");
   uint32_t slot0;
   int nch, ntile, t0n, t1n, n0, n1, n2;
   bool ok;
@@ -597,7 +616,7 @@ struct GemvPlan {
       for (int it = 0; it < PIT; ++it)
 #pragma unroll
         for (int t = 0; t < MAXT; ++t)
-          if (t < ntile)
+          if (t < ntile && (!kRag || warp + it * kConsumerWarps < KS))
             ldmatrix_x4(abase[t] + (warp + it * kConsumerWarps) * 32, pa[it][t][0], pa[it][t][1],
                         pa[it][t][2], pa[it][t][3]);
     }
@@ -620,6 +639,7 @@ struct GemvPlan {
 #pragma unroll
       for (int it = 0; it < PIT; ++it) {
         const int ks = warp + it * kConsumerWarps;
+        if (kRag && ks >= KS) break;
         const uint32_t b0 = g < 3 ? xs0[ks * 8 + tq] : 0u;
         const uint32_t b1 = g < 3 ? xs0[ks * 8 + tq + 4] : 0u;
 #pragma unroll
@@ -637,6 +657,7 @@ struct GemvPlan {
 #pragma unroll 2
       for (int it = PIT; it < ITER; ++it) {
         const int ks = warp + it * kConsumerWarps;
+        if (kRag && ks >= KS) break;
         const uint32_t b0 = g < 3 ? xs0[ks * 8 + tq] : 0u;
         const uint32_t b1 = g < 3 ? xs0[ks * 8 + tq + 4] : 0u;
 #pragma unroll
@@ -739,6 +760,46 @@ __device__ __forceinline__ float hop_to_xs(const KParams& P, Smem<S>& sm, const 
         if (GAIN) x = gr.g[k < GainRegs<S>::kPer ? k : 0] * v;
         split_one(sm, i, x);
       }
+    }
+  }
+  return ss;
+}
+
+// Tensor-parallel layer input: x = x' + sum over ranks (in rank order, so
+// every GPU computes the same fp32 value) of each rank's partial down
+// projection, read from the TP slots src[j * H + i] that the ranks write over
+// NVLink.  x' (the residual after attention) is in xres and is replaced by x.
+// With SPLIT the (gain-scaled) x is also staged for the next GEMV as in
+// hop_to_xs.  Returns this thread's sum of x^2.
+template <class S, int TP, bool SPLIT>
+__device__ __forceinline__ float hop_sum_to_xs(const KParams& P, Smem<S>& sm, const uint64_t* src,
+                                               uint32_t tag, const GainRegs<S>& gr) {
+  constexpr int PER = GainRegs<S>::kPer;
+  static_assert(S::H % kConsumerThreads == 0, "whole rows per thread");
+  // At most 16 words in flight per thread (registers); TP = 8 takes two rounds.
+  constexpr int EG = PER * TP <= 16 ? PER : 16 / TP;
+  float ss = 0.f;
+#pragma unroll
+  for (int e0 = 0; e0 < PER; e0 += EG) {
+    uint64_t w[EG * TP];
+    const uint64_t* sp[EG * TP];
+#pragma unroll
+    for (int e = 0; e < EG; ++e)
+#pragma unroll
+      for (int j = 0; j < TP; ++j) {
+        sp[e * TP + j] = src + (size_t)j * S::H + threadIdx.x + (e0 + e) * kConsumerThreads;
+        w[e * TP + j] = ld_relaxed_sys(sp[e * TP + j]);
+      }
+    resolve_tagged<S, EG * TP, true>(P, sm, w, sp, EG * TP, tag);
+#pragma unroll
+    for (int e = 0; e < EG; ++e) {
+      const int i = threadIdx.x + (e0 + e) * kConsumerThreads;
+      float v = sm.xres[i];
+#pragma unroll
+      for (int j = 0; j < TP; ++j) v += __uint_as_float((uint32_t)w[e * TP + j]);
+      sm.xres[i] = v;
+      ss = fmaf(v, v, ss);
+      if (SPLIT) split_one(sm, i, gr.g[e0 + e] * v);
     }
   }
   return ss;
@@ -1147,9 +1208,14 @@ __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, u
   }
 }
 
-template <class S>
+template <class S, int TP>
 __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, int cta) {
   const int N = P.ncta, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Tensor parallelism (TP > 1): this GPU computes the MLP rows [rank IR,
+  // (rank + 1) IR) and the LM-head rows [rank VR, (rank + 1) VR); attention
+  // and the O projection are replicated on every GPU.
+  constexpr int IR = S::I / TP, VR = S::V / TP;
+  const int rank = TP > 1 ? P.tp_rank : 0;
   uint32_t kc = 0;
   int tok = P.forced[0];
   #pragma unroll 1
@@ -1186,8 +1252,12 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         gp.prepare(P, sm, ring, kc, rq[0], rq[1], rq[2]);
         float ss = 0.f;
         if (l > 0) {
-          ss = hop_to_xs<S, true, true, GainRegs<S>::kPer>(P, sm, P.hop + HopLayout<S>::X + (size_t)(l & 1) * S::H, S::H,
-                                        tag_of(seq, l - 1, 4), gains);
+          if constexpr (TP == 1)
+            ss = hop_to_xs<S, true, true, GainRegs<S>::kPer>(P, sm, P.hop + HopLayout<S>::X + (size_t)(l & 1) * S::H, S::H,
+                                          tag_of(seq, l - 1, 4), gains);
+          else
+            ss = hop_sum_to_xs<S, TP, true>(P, sm, P.hop + HopLayout<S, TP>::X + (size_t)(l & 1) * TP * S::H,
+                                            tag_of(seq, l - 1, 4), gains);
         } else {
 #pragma unroll
           for (int e = 0; e < GainRegs<S>::kPer; ++e) {
@@ -1246,7 +1316,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
       {
         gains.load(wptr(l, W_FFN_NORM));
         int r0, r1;
-        split_rows(S::I, N, cta, phase_rot(l, 2, N), r0, r1);
+        split_rows(IR, N, cta, phase_rot(l, 2, N), r0, r1);
         GemvPlan<S, S::H, 4> gp;
         gp.prepare(P, sm, ring, kc, r1 - r0, r1 - r0, 0);
         // xres is rewritten by the hop below: every thread must be done with
@@ -1273,9 +1343,9 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
       {
         int r0, r1;
         split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
-        GemvPlan<S, S::I, 2> gp;
+        GemvPlan<S, IR, 2> gp;
         gp.prepare(P, sm, ring, kc, r1 - r0, 0, 0);
-        hop_to_xs<S, false, false, (S::I + kConsumerThreads - 1) / kConsumerThreads>(P, sm, P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I, S::I,
+        hop_to_xs<S, false, false, (IR + kConsumerThreads - 1) / kConsumerThreads>(P, sm, P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I, IR,
                                    tag_of(seq, l, 3), gains);
         if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
         MK_DP(17);
@@ -1284,9 +1354,21 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         uint64_t* dst = P.hop + HopLayout<S>::X + (size_t)((l + 1) & 1) * S::H;
         const uint32_t tg = tag_of(seq, l, 4);
         const bool skip = (l == 0 && cta == P.debug_skip_cta);
-        if (!skip)
-          for (int r = tid; r < r1 - r0; r += kConsumerThreads)
-            st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
+        if constexpr (TP == 1) {
+          if (!skip)
+            for (int r = tid; r < r1 - r0; r += kConsumerThreads)
+              st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
+        } else {
+          // This rank's partial rows (no residual: every rank adds x' itself)
+          // into slot `rank` of every GPU's X hop, over NVLink for the peers.
+          (void)dst;
+          const size_t off = HopLayout<S, TP>::X + (size_t)((l + 1) & 1) * TP * S::H + (size_t)rank * S::H + r0;
+          if (!skip)
+            for (int r = tid; r < r1 - r0; r += kConsumerThreads)
+#pragma unroll
+              for (int j = 0; j < TP; ++j)
+                st_tagged_sys(P.peer_hop[j] + off + r, tg, __float_as_uint(sm.rowsum[0][r]));
+        }
         // xres is rewritten by the next layer's hop: finish the reads first.
         consumer_sync(kConsumerThreads);
         if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 6);
@@ -1303,47 +1385,86 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
     appended = false;
     GainRegs<S> fgains;
     fgains.load(sm.wtab[1]);
-    wait_tagged(P, sm, P.hop + HopLayout<S>::X + (size_t)(S::L & 1) * S::H, S::H,
-                tag_of(seq, S::L - 1, 4), sm.xres);
+    if constexpr (TP == 1)
+      wait_tagged(P, sm, P.hop + HopLayout<S>::X + (size_t)(S::L & 1) * S::H, S::H,
+                  tag_of(seq, S::L - 1, 4), sm.xres);
+    else
+      hop_sum_to_xs<S, TP, false>(P, sm, P.hop + HopLayout<S, TP>::X + (size_t)(S::L & 1) * TP * S::H,
+                                  tag_of(seq, S::L - 1, 4), fgains);
     if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
     rmsnorm_to_xin(sm, fgains);
     if (tid == 0) trace_point<S>(P, t, cta, 7 * S::L);
     {
       int r0, r1;
-      split_rows(S::V, N, cta, phase_rot(S::L, 4, N), r0, r1);
+      split_rows(VR, N, cta, phase_rot(S::L, 4, N), r0, r1);
+      r0 += rank * VR;
+      r1 += rank * VR;
       float bv = -INFINITY;
       int bi = 0x7fffffff;
       float* lrow = P.logits ? P.logits + (size_t)t * S::V : nullptr;
       kc += lm_rows<S>(P, sm, ring, kc, r0, r1, lrow, bv, bi);
       if (lane == 0) { sm.red[warp] = bv; sm.redi[warp] = bi; }
       consumer_sync(kConsumerThreads);
-      uint64_t* lm = P.hop + HopLayout<S>::LM + (size_t)(t & 1) * kMaxCtas * 2;
+      // (max, index) pair of CTA c of rank j at slot j * N + c.
+      const size_t lm_off = HopLayout<S, TP>::LM + (size_t)(t & 1) * TP * kMaxCtas * 2;
+      uint64_t* lm = P.hop + lm_off;
       const uint32_t tg = tag_of(seq, S::L, 0);
       if (tid == 0) {
         float v = sm.red[0];
         int ix = sm.redi[0];
         for (int w = 1; w < kConsumerWarps; ++w)
           if (sm.red[w] > v || (sm.red[w] == v && sm.redi[w] < ix)) { v = sm.red[w]; ix = sm.redi[w]; }
-        st_tagged(lm + 2 * cta, tg, __float_as_uint(v));
-        st_tagged(lm + 2 * cta + 1, tg, (uint32_t)ix);
+        if constexpr (TP == 1) {
+          st_tagged(lm + 2 * cta, tg, __float_as_uint(v));
+          st_tagged(lm + 2 * cta + 1, tg, (uint32_t)ix);
+        } else {
+          const size_t slot = (size_t)rank * N + cta;
+#pragma unroll
+          for (int j = 0; j < TP; ++j) {
+            st_tagged_sys(P.peer_hop[j] + lm_off + 2 * slot, tg, __float_as_uint(v));
+            st_tagged_sys(P.peer_hop[j] + lm_off + 2 * slot + 1, tg, (uint32_t)ix);
+          }
+        }
         trace_point<S>(P, t, cta, 7 * S::L + 1);
       }
       // Every CTA reduces all CTAs' (max, index) pairs: lowest index wins ties.
-      float* pairs = &sm.partw[0][0];
-      for (int c = tid; c < N; c += kConsumerThreads) {
-        uint64_t w2[2] = {ld_relaxed(lm + 2 * c), ld_relaxed(lm + 2 * c + 1)};
-        const uint64_t* sp2[2] = {lm + 2 * c, lm + 2 * c + 1};
-        resolve_tagged<S, 2>(P, sm, w2, sp2, 2, tg);
-        pairs[c] = __uint_as_float((uint32_t)w2[0]);
-        pairs[kMaxCtas + c] = __uint_as_float((uint32_t)w2[1]);
-      }
-      consumer_sync(kConsumerThreads);
-      if (warp == 0) {
+      if constexpr (TP == 1) {
+        float* pairs = &sm.partw[0][0];
+        for (int c = tid; c < N; c += kConsumerThreads) {
+          uint64_t w2[2] = {ld_relaxed(lm + 2 * c), ld_relaxed(lm + 2 * c + 1)};
+          const uint64_t* sp2[2] = {lm + 2 * c, lm + 2 * c + 1};
+          resolve_tagged<S, 2>(P, sm, w2, sp2, 2, tg);
+          pairs[c] = __uint_as_float((uint32_t)w2[0]);
+          pairs[kMaxCtas + c] = __uint_as_float((uint32_t)w2[1]);
+        }
+        consumer_sync(kConsumerThreads);
+        if (warp == 0) {
+          float v = -INFINITY;
+          int ix = 0x7fffffff;
+          for (int c = lane; c < N; c += 32) {
+            const float cv = pairs[c];
+            const int ci = (int)__float_as_uint(pairs[kMaxCtas + c]);
+            if (cv > v || (cv == v && ci < ix)) { v = cv; ix = ci; }
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+            if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
+          }
+          if (lane == 0) sm.next_token = ix;
+        }
+      } else {
+        // TP * N pairs (all ranks): a running best per thread, then per warp,
+        // then across the warps.
         float v = -INFINITY;
         int ix = 0x7fffffff;
-        for (int c = lane; c < N; c += 32) {
-          const float cv = pairs[c];
-          const int ci = (int)__float_as_uint(pairs[kMaxCtas + c]);
+        for (int c = tid; c < TP * N; c += kConsumerThreads) {
+          uint64_t w2[2] = {ld_relaxed_sys(lm + 2 * c), ld_relaxed_sys(lm + 2 * c + 1)};
+          const uint64_t* sp2[2] = {lm + 2 * c, lm + 2 * c + 1};
+          resolve_tagged<S, 2, true>(P, sm, w2, sp2, 2, tg);
+          const float cv = __uint_as_float((uint32_t)w2[0]);
+          const int ci = (int)(uint32_t)w2[1];
           if (cv > v || (cv == v && ci < ix)) { v = cv; ix = ci; }
         }
 #pragma unroll
@@ -1352,7 +1473,18 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
           const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
           if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
         }
-        if (lane == 0) sm.next_token = ix;
+        // sm.red / redi were last read by thread 0 before its publish above.
+        consumer_sync(kConsumerThreads);
+        if (lane == 0) { sm.red[warp] = v; sm.redi[warp] = ix; }
+        consumer_sync(kConsumerThreads);
+        if (tid == 0) {
+          for (int w = 1; w < kConsumerWarps; ++w)
+            if (sm.red[w] > sm.red[0] || (sm.red[w] == sm.red[0] && sm.redi[w] < sm.redi[0])) {
+              sm.red[0] = sm.red[w];
+              sm.redi[0] = sm.redi[w];
+            }
+          sm.next_token = sm.redi[0];
+        }
       }
       if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
       const int best = sm.next_token;
@@ -1374,8 +1506,10 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
   }
 }
 
-template <class S>
+template <class S, int TP = 1>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ KParams P) {
+  static_assert(TP >= 1 && TP <= kMaxTP && S::I % TP == 0 && S::V % TP == 0 && (S::I / TP) % 16 == 0,
+                "tensor-parallel split");
   extern __shared__ __align__(128) uint8_t dsm[];
   uint8_t* ring = dsm;
   Smem<S>& sm = *reinterpret_cast<Smem<S>*>(dsm + (size_t)S::NST * S::STB);
@@ -1398,10 +1532,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   // consumer warpgroups.
   if (threadIdx.x >= kConsumerThreads) {
     setmaxnreg_dec<kProducerRegs>();
-    if (threadIdx.x < kConsumerThreads + 32) producer<S>(sm.prm, sm, ring, cta);
+    if (threadIdx.x < kConsumerThreads + 32) producer<S, TP>(sm.prm, sm, ring, cta);
   } else {
     setmaxnreg_inc<kConsumerRegs>();
-    consumers<S>(sm.prm, sm, ring, cta);
+    consumers<S, TP>(sm.prm, sm, ring, cta);
   }
 }
 

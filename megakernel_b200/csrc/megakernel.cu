@@ -58,9 +58,24 @@ struct State {
   const void* d_weights = nullptr;       // caller's weight buffer and offsets (parallel prefill)
   std::vector<long long> offsets;
   void* prefill = nullptr;               // lazily built batched state bound to d_kv (batch.cu)
+  // Tensor parallelism (megakernel_tp_*): rank, size, and every rank's hop
+  // buffer (own at [tp_rank], peers mapped by CUDA IPC).
+  int tp_rank = 0;
+  int tp_size = 1;
+  bool tp_connected = false;
+  uint64_t* peer_hop[mk::kMaxTP] = {};
+  bool peer_opened[mk::kMaxTP] = {};
 };
 
 void prefill_free(void* p);   // batch.cu
+
+}  // namespace
+
+namespace mk_tp {
+const void* kernel(int shape_id, int tp, size_t* hop_words);   // tp.cu
+}
+
+namespace {
 
 struct ShapeInfo {
   int H, L, NQ, NKV, D, I, V;
@@ -146,6 +161,8 @@ void kernel_info(State* st) {
 
 void free_state(State* st) {
   if (!st) return;
+  for (int j = 0; j < mk::kMaxTP; ++j)
+    if (st->peer_opened[j]) cudaIpcCloseMemHandle(st->peer_hop[j]);
   cudaFree(st->d_wptr);
   cudaFree(st->d_kv);
   cudaFree(st->d_cos);
@@ -184,9 +201,10 @@ int infer_shape(const long long* off, int n) {
 namespace {
 
 int init_impl(void* d_weights, const long long* offsets, int num_offsets, const mk_options* o,
-              State** out) {
+              State** out, int tp_rank = 0, int tp_size = 1) {
   *out = nullptr;
   if (!d_weights || !offsets) return MK_ERR_INVALID_ARG;
+  if (tp_size < 1 || tp_size > mk::kMaxTP || tp_rank < 0 || tp_rank >= tp_size) return MK_ERR_INVALID_ARG;
   const int id = o->shape_id >= 0 ? o->shape_id : infer_shape(offsets, num_offsets);
   if (id < 0 || id >= kNumShapes) return MK_ERR_SHAPE;
   const ShapeInfo s = shape_info(id);
@@ -214,6 +232,14 @@ int init_impl(void* d_weights, const long long* offsets, int num_offsets, const 
     case 0: kernel_info<mk::ShapeD64>(st); break;
     case 1: kernel_info<mk::ShapeD128>(st); break;
     default: kernel_info<mk::ShapeTiny>(st); break;
+  }
+  st->tp_rank = tp_rank;
+  st->tp_size = tp_size;
+  if (tp_size > 1) {
+    size_t words = 0;
+    st->kernel = mk_tp::kernel(id, tp_size, &words);
+    if (!st->kernel) return bail(MK_ERR_INVALID_ARG);   // (shape, TP size) not compiled
+    st->hop_bytes = words * 8;
   }
   int sms = 0, coop = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
@@ -280,7 +306,11 @@ int init_impl(void* d_weights, const long long* offsets, int num_offsets, const 
 // One cooperative launch of n_steps steps; asynchronous on `stream`.
 int launch(State* st, const int* d_forced, int n_forced, int n_steps, int* d_out,
            float* d_logits, cudaStream_t stream) {
+  if (st->tp_size > 1 && !st->tp_connected) return MK_ERR_INVALID_ARG;
   if (st->seq + (uint32_t)n_steps >= kSeqLimit) {
+    // Peers write into this GPU's hop buffer whenever they run ahead, so a
+    // tensor-parallel engine cannot clear it on its own.
+    if (st->tp_size > 1) return MK_ERR_CAPACITY;
     // Tag sequence numbers are 24 bits: start over from clean buffers.
     MK_CUDA(cudaMemsetAsync(st->d_hop, 0, st->hop_bytes, stream));
     st->seq = 1;
@@ -308,6 +338,8 @@ int launch(State* st, const int* d_forced, int n_forced, int n_steps, int* d_out
   P.trace = st->d_trace;
   P.trace_steps = st->d_trace ? st->trace_steps : 0;
   P.detail = st->d_detail;
+  P.tp_rank = st->tp_rank;
+  for (int j = 0; j < mk::kMaxTP; ++j) P.peer_hop[j] = st->peer_hop[j];
   MK_CUDA(cudaMemsetAsync(st->d_err, 0, sizeof(int), stream));
   void* args[] = {&P};
   cudaError_t e = cudaLaunchCooperativeKernel(st->kernel, dim3(st->ncta), dim3(mk::kThreads), args,
@@ -459,7 +491,9 @@ int megakernel_decode_n(void* handle, const int* d_tokens, int n_forced, int n_s
   if (!d_tokens || !d_out || n_forced < 1 || n_steps < 1 || n_forced > n_steps)
     return set_err(st, MK_ERR_INVALID_ARG);
   if (cudaSetDevice(st->device) != cudaSuccess) return set_err(st, MK_ERR_CUDA);
-  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : st->stream;
+  // NULL: the default stream, as the reference's calls use, so the launch is
+  // ordered after the caller's earlier default-stream work on its buffers.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   return set_err(st, run_sync(st, d_tokens, n_forced, n_steps, d_out, d_logits, s));
 }
 
@@ -594,6 +628,62 @@ int megakernel_set_trace_detail(void* handle, void* d_buf) {
   State* st = as_state(handle);
   if (!st) return MK_ERR_INVALID_ARG;
   st->d_detail = static_cast<uint64_t*>(d_buf);
+  return MK_OK;
+}
+
+int megakernel_tp_init(void* d_weights, const long long* offsets, int num_offsets,
+                       const mk_options* opts, int tp_rank, int tp_size, void** out_handle) {
+  if (!out_handle) return MK_ERR_INVALID_ARG;
+  *out_handle = nullptr;
+  if (tp_size < 2) return MK_ERR_INVALID_ARG;
+  mk_options def;
+  megakernel_default_options(&def);
+  State* st = nullptr;
+  const int rc = init_impl(d_weights, offsets, num_offsets, opts ? opts : &def, &st, tp_rank, tp_size);
+  if (rc == MK_OK) *out_handle = st;
+  return rc;
+}
+
+int megakernel_tp_ipc_handle(void* handle, void* out) {
+  State* st = as_state(handle);
+  if (!st || !out || st->tp_size < 2) return MK_ERR_INVALID_ARG;
+  MK_CUDA(cudaSetDevice(st->device));
+  cudaIpcMemHandle_t h;
+  MK_CUDA(cudaIpcGetMemHandle(&h, st->d_hop));
+  std::memcpy(out, &h, sizeof(h));
+  return MK_OK;
+}
+
+int megakernel_tp_connect(void* handle, const void* handles) {
+  State* st = as_state(handle);
+  if (!st || !handles || st->tp_size < 2 || st->tp_connected) return MK_ERR_INVALID_ARG;
+  MK_CUDA(cudaSetDevice(st->device));
+  for (int j = 0; j < st->tp_size; ++j) {
+    if (j == st->tp_rank) {
+      st->peer_hop[j] = st->d_hop;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(handles) + (size_t)j * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      std::fprintf(stderr, "megakernel: cudaIpcOpenMemHandle(rank %d) failed: %s\n", j, cudaGetErrorString(e));
+      cudaGetLastError();
+      return MK_ERR_CUDA;
+    }
+    st->peer_hop[j] = static_cast<uint64_t*>(p);
+    st->peer_opened[j] = true;
+  }
+  st->tp_connected = true;
+  return MK_OK;
+}
+
+int megakernel_tp_info(void* handle, int* rank, int* size) {
+  State* st = as_state(handle);
+  if (!st || !rank || !size) return MK_ERR_INVALID_ARG;
+  *rank = st->tp_rank;
+  *size = st->tp_size;
   return MK_OK;
 }
 

@@ -79,6 +79,17 @@ __device__ __forceinline__ uint64_t ld_relaxed(const uint64_t* p) {
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// System-scope forms for words that cross GPUs (stores into a peer's buffer
+// over NVLink, and the loads that poll for them).
+__device__ __forceinline__ void st_tagged_sys(uint64_t* p, uint32_t tag, uint32_t payload) {
+  uint64_t v = (static_cast<uint64_t>(tag) << 32) | payload;
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ int ld_volatile_i32(const int* p) {
   int v;
   asm volatile("ld.volatile.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -24,6 +24,7 @@ constexpr int kRingBytes = 176 * 1024;
 constexpr int kMaxCtas = 256;
 constexpr int kRowsMax = 256;           // weight rows one CTA owns in one phase
 constexpr int kRowPad = 16;             // bytes between weight rows in a ring stage
+constexpr int kMaxTP = 8;               // tensor-parallel GPUs at most
 constexpr int kMaxChunksPerHead = 16;   // attention split-KV chunks per KV head
 // Fewest cached positions per chunk: below this a chunk's fixed costs (q/k/v
 // wait, QK-norm, RoPE, partial publish) outweigh the positions it walks.

@@ -1,7 +1,7 @@
 // Inline-PTX primitives for the batched path on sm_100a: tcgen05 (TMEM
 // allocation, MMA, commit, loads, fences) and 2-D TMA tensor loads.
 //
-// No load here uses .multicast::cluster, and no tensor map points at another
+// Every load here is a plain (single-CTA) copy, and no tensor map points at another
 // GPU's memory.
 #pragma once
 #include <cstdint>

@@ -72,6 +72,14 @@ class Shape:
             n += 2 * c
         return n
 
+    def tp_weight_bytes(self, tp: int) -> int:
+        """Weight bytes one GPU streams per token under tensor parallelism over
+        `tp` GPUs: attention (norms, QKV, O) and the final norm replicated,
+        the MLP matrices and the LM head (tied embedding) split `tp` ways."""
+        mlp = 3 * 2 * self.intermediate * self.hidden * self.layers
+        lm = 2 * self.vocab * self.hidden
+        return self.weight_bytes - mlp - lm + (mlp + lm) // tp
+
     @property
     def kv_bytes_per_position(self) -> int:
         """bf16 K and V bytes for one position across all layers."""
