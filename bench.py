@@ -251,7 +251,10 @@ def run_ours(args, world, rank, local):
         "cpu_baseline": cpu,
     }
     if world > 1 and not args.no_tp:
-        line["tensor_parallel"] = run_tp(args, world, rank, local, shape, flat, offs, prompt, check)
+        try:
+            line["tensor_parallel"] = run_tp(args, world, rank, local, shape, flat, offs, prompt, check)
+        except RuntimeError as e:  # reported, never allowed to drop the headline line
+            line["tensor_parallel"] = {"error": str(e)[:200]}
     if rank == 0 and world == 1 and not args.no_batched:
         line["long_context"] = run_long(shape, flat, offs, dev, peak)
         line["batched"] = run_batched(shape, flat, offs, dev, peak)
