@@ -36,10 +36,13 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s, Qwen3-0.6B shape, B=1 on 1×B200; % of HBM roofline"
 PROMPT, GEN = 128, 512
-# DRAM bytes (read + write) per decoded token of the decode kernel, from the
-# ncu capture summarised in profiles/decode_kernel_d64_b1.md (2-step launch
-# at positions 0-1: 1.944 GB read + 4.0 MB written per 2 tokens, per token).
-NCU_TRAFFIC_PER_TOKEN = 973_941_000
+# Measured DRAM traffic of the decode kernel relative to its algorithmic bytes,
+# from the ncu capture summarised in profiles/decode_kernel_d64_b1.md (one
+# launch of 2 tokens at positions 128-129: 1.958796 GB read + 3.49696 MB
+# written against 979,346,432 + 979,403,776 algorithmic bytes).  The launch's traffic is
+# scaled from it by the algorithmic bytes of the timed launch (traffic grows
+# with the K/V bytes the same way).
+NCU_TRAFFIC_RATIO = (1_958_796_000 + 3_496_960) / (979_346_432 + 979_403_776)
 
 
 def load_peaks():
@@ -231,7 +234,7 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tps, cores, sample = cpu_reference(shape, w, prompt, n_new=args.ref_tokens)
         cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample}
-    traffic = NCU_TRAFFIC_PER_TOKEN * GEN if NCU_TRAFFIC_PER_TOKEN else None
+    traffic = int(NCU_TRAFFIC_RATIO * bytes_launch)
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
