@@ -121,7 +121,7 @@ int megakernel_set_trace_detail(void* handle, void* d_buf);
 /* ---- decode without device allocation ------------------------------------ */
 
 #define MK_NOALLOC_MAX_POS 2048           /* pos + n_steps must not exceed this */
-#define MK_NOALLOC_SCRATCH_BYTES 916224   /* static device scratch per GPU */
+#define MK_NOALLOC_SCRATCH_BYTES 932608   /* static device scratch per GPU */
 
 /* No counterpart in the reference.  For callers that cannot allocate device
  * memory (a runtime that owns all device allocations, an allocator-free

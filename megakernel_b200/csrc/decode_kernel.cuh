@@ -43,6 +43,9 @@
 #ifndef MK_GEMV_PIT
 #define MK_GEMV_PIT 2
 #endif
+#ifndef MK_DBG_ATT
+#define MK_DBG_ATT 0
+#endif
 // Pause between polling rounds of a tagged-word wait (ns).
 #ifndef MK_POLL_BACKOFF_NS
 #define MK_POLL_BACKOFF_NS 200
@@ -107,7 +110,8 @@ struct HopLayout {
   static constexpr long long HM = XA + 2 * S::H;           // [2][I]  silu(g)*u
   static constexpr long long X = HM + 2 * S::I;            // [2][TP][H]  layer input
   static constexpr long long LM = X + 2LL * TP * S::H;     // [2][TP * kMaxCtas][2]
-  static constexpr long long TOTAL = LM + 2LL * TP * kMaxCtas * 2;
+  static constexpr long long MH = LM + 2LL * TP * kMaxCtas * 2;  // [2][Q]  merged heads (two-level merge)
+  static constexpr long long TOTAL = MH + 2LL * S::Q;
 };
 
 // Tag of phase `k` (0 qkv, 1 att, 2 xa, 3 hm, 4 x-out) of layer `l` at step seq.
@@ -151,7 +155,7 @@ struct Smem {
   float rowsum[2][kRowsMax];          // GEMV results of this CTA's rows
   alignas(16) float qs[S::GRP][S::D];     // normed + roped queries (read as float4)
   float sc[S::GRP][S::SUBP + 2];      // scores / probabilities of one block
-  float pv[kConsumerThreads];         // PV partials (parts x GRP x D)
+  float pv[kPvParts * S::GRP * S::D];  // PV partials [part][GRP][D]
   float mrun[S::GRP], lrun[S::GRP], corr[S::GRP];
   float gq[S::D], gk[S::D];           // q_norm / k_norm gains of the layer
   float rc[S::D / 2], rs[S::D / 2];   // RoPE cos / sin row of position p
@@ -889,12 +893,16 @@ namespace mk {
 template <class S>
 __device__ MK_PHASE void attend_block(Smem<S>& sm, const __nv_bfloat16* K1, const __nv_bfloat16* V1,
                                           int n1, const __nv_bfloat16* K2, const __nv_bfloat16* V2,
-                                          int n2, float& acc) {
+                                          int n2, float (&acc)[S::D / 32]) {
   constexpr int D = S::D, GRP = S::GRP;
   constexpr int PIECES = D / 8;  // 16-byte pieces per row
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = n1 + n2;
   const float scale = (D == 64) ? 0.125f : 0.08838834764831845f;  // D^-0.5
+#if MK_DBG_ATT == 1
+  for (int i = threadIdx.x; i < GRP * n; i += kConsumerThreads) sm.sc[i / n][i % n] = 0.f;
+  if (false)
+#endif
   for (int i = threadIdx.x; i < GRP * n; i += kConsumerThreads) {
     const int g = i / n, pos = i - g * n;
     const __nv_bfloat16* kr = pos < n1 ? K1 + (size_t)pos * D : K2 + (size_t)(pos - n1) * D;
@@ -918,6 +926,10 @@ __device__ MK_PHASE void attend_block(Smem<S>& sm, const __nv_bfloat16* K1, cons
     sm.sc[g][pos] = (s0 + s1) * scale;
   }
   consumer_sync(kConsumerThreads);
+#if MK_DBG_ATT == 2
+  if (warp < GRP && lane == 0) { sm.corr[warp] = 1.f; }
+  if (false)
+#endif
   if (warp < GRP) {
     const int g = warp;
     float mx = -INFINITY;
@@ -942,22 +954,36 @@ __device__ MK_PHASE void attend_block(Smem<S>& sm, const __nv_bfloat16* K1, cons
   }
   consumer_sync(kConsumerThreads);
   {
-    constexpr int GD = GRP * D;
-    constexpr int PARTS = kConsumerThreads / GD;
-    const int tid = threadIdx.x;
-    const int part = tid / GD, g = (tid / D) % GRP, d = tid % D;
-    float a0 = 0.f, a1 = 0.f;
+    // P.V: warp w takes query head w % GRP and every kPvParts-th position
+    // starting at w / GRP; lane l the DPL dims [l DPL, (l+1) DPL), loaded as
+    // bf16 pairs (one 4- or 8-byte load per position and lane).
+    constexpr int DPL = D / 32;
+    const int g = warp % GRP, part = warp / GRP, d0 = lane * DPL;
+    float a[DPL], b[DPL];
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) a[k] = b[k] = 0.f;
+    auto fma_row = [&](float (&c)[DPL], float pw, const __nv_bfloat16* vr) {
+#pragma unroll
+      for (int k = 0; k < DPL; k += 2) {
+        const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vr + d0 + k));
+        c[k] = fmaf(pw, v.x, c[k]);
+        c[k + 1] = fmaf(pw, v.y, c[k + 1]);
+      }
+    };
     int pos = part;
+#if MK_DBG_ATT == 3
+    pos = n;
+#endif
 #pragma unroll 4
-    for (; pos + PARTS < n1; pos += 2 * PARTS) {
-      a0 = fmaf(sm.sc[g][pos], __bfloat162float(V1[(size_t)pos * D + d]), a0);
-      a1 = fmaf(sm.sc[g][pos + PARTS], __bfloat162float(V1[(size_t)(pos + PARTS) * D + d]), a1);
+    for (; pos + kPvParts < n1; pos += 2 * kPvParts) {
+      fma_row(a, sm.sc[g][pos], V1 + (size_t)pos * D);
+      fma_row(b, sm.sc[g][pos + kPvParts], V1 + (size_t)(pos + kPvParts) * D);
     }
-    for (; pos < n; pos += PARTS) {
-      const __nv_bfloat16 v = pos < n1 ? V1[(size_t)pos * D + d] : V2[(size_t)(pos - n1) * D + d];
-      a0 = fmaf(sm.sc[g][pos], __bfloat162float(v), a0);
-    }
-    acc = acc * sm.corr[g] + (a0 + a1);
+    for (; pos < n; pos += kPvParts)
+      fma_row(a, sm.sc[g][pos], pos < n1 ? V1 + (size_t)pos * D : V2 + (size_t)(pos - n1) * D);
+    const float c = sm.corr[g];
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) acc[k] = acc[k] * c + (a[k] + b[k]);
   }
   consumer_sync(kConsumerThreads);
 }
@@ -1075,7 +1101,9 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
   consumer_sync(kConsumerThreads);
   MK_DP(5);
 
-  float acc = 0.f;
+  float acc[D / 32];
+#pragma unroll
+  for (int k = 0; k < D / 32; ++k) acc[k] = 0.f;
   // Positions held outside the ring -- p-1 (slot 0) and the current p (slot
   // 1) -- ride along with the first ring block (or form the only block).
   const int s0 = prev ? 0 : 1;
@@ -1101,16 +1129,22 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
     kc += 2;
   }
   MK_DP(7);
-  sm.pv[tid] = acc;
+  {
+    // This warp's head / part / dims, as attend_block's P.V assigns them.
+    constexpr int DPL = D / 32;
+    float* dst = &sm.pv[((warp / GRP) * GRP + warp % GRP) * D + lane * DPL];
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) dst[k] = acc[k];
+  }
   consumer_sync(kConsumerThreads);
   uint64_t* out = P.hop + HopLayout<S>::ATT + (size_t)(l & 1) * HopLayout<S>::kAttWords +
                   (size_t)item * GRP * (D + 2);
   const uint32_t ta = tag_of(seq, l, 1);
   if (tid < GRP * D) {
-    constexpr int GD = GRP * D, PARTS = kConsumerThreads / GD;
+    constexpr int GD = GRP * D;
     float s = 0.f;
 #pragma unroll
-    for (int q = 0; q < PARTS; ++q) s += sm.pv[q * GD + tid];
+    for (int q = 0; q < kPvParts; ++q) s += sm.pv[q * GD + tid];
     const int g = tid / D, d = tid % D;
     st_tagged(out + g * (D + 2) + d, ta, __float_as_uint(s));
   }
@@ -1132,15 +1166,90 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
   return kc - kc0;
 }
 
+// Two-level merge (nc >= kMerge2MinChunks): the CTA that walked chunk 0 of KV
+// head h merges the nc partials of that head's GRP query heads and publishes
+// the GRP x D results to the MH hop, so the other CTAs read Q words instead of
+// every partial (at 16 chunks the direct merge had each of 148 CTAs read
+// 135 KB of partials, about 9 us per layer).  Called after all of this CTA's
+// items of the layer, so it never waits on a partial this CTA has yet to make.
+template <class S>
+__device__ MK_PHASE void merge_head(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc, int h) {
+  constexpr int D = S::D, GRP = S::GRP;
+  static_assert(GRP * kMaxChunksPerHead <= kConsumerThreads && GRP * D <= kConsumerThreads, "merge_head");
+  const int tid = threadIdx.x;
+  const uint64_t* att = P.hop + HopLayout<S>::ATT + (size_t)(l & 1) * HopLayout<S>::kAttWords +
+                        (size_t)h * nc * GRP * (D + 2);
+  const uint32_t ta = tag_of(seq, l, 1);
+  if (tid < GRP * nc) {
+    const int g = tid / nc, j = tid % nc;
+    const uint64_t* bj = att + ((size_t)j * GRP + g) * (D + 2) + D;
+    uint64_t w2[2] = {ld_relaxed(bj), ld_relaxed(bj + 1)};
+    const uint64_t* sp2[2] = {bj, bj + 1};
+    resolve_tagged<S, 2>(P, sm, w2, sp2, 2, ta);
+    sm.mlbuf[2 * tid] = __uint_as_float((uint32_t)w2[0]);
+    sm.mlbuf[2 * tid + 1] = __uint_as_float((uint32_t)w2[1]);
+  }
+  consumer_sync(kConsumerThreads);
+  if (tid < GRP * D) {
+    const int g = tid / D, dd = tid % D;
+    uint64_t w[kMaxChunksPerHead];
+    const uint64_t* sp[kMaxChunksPerHead];
+#pragma unroll
+    for (int j = 0; j < kMaxChunksPerHead; ++j) {
+      sp[j] = att + ((size_t)j * GRP + g) * (D + 2) + dd;
+      w[j] = j < nc ? ld_relaxed(sp[j]) : 0;
+    }
+    resolve_tagged<S, kMaxChunksPerHead>(P, sm, w, sp, nc, ta);
+    float M = -INFINITY;
+    for (int j = 0; j < nc; ++j) M = fmaxf(M, sm.mlbuf[2 * (g * nc + j)]);
+    float den = 0.f, acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxChunksPerHead; ++j) {
+      if (j < nc) {
+        const float cj = expf(sm.mlbuf[2 * (g * nc + j)] - M);
+        den = fmaf(sm.mlbuf[2 * (g * nc + j) + 1], cj, den);
+        acc = fmaf(__uint_as_float((uint32_t)w[j]), cj, acc);
+      }
+    }
+    st_tagged(P.hop + HopLayout<S>::MH + (size_t)(l & 1) * S::Q + (size_t)(h * GRP + g) * D + dd, ta,
+              __float_as_uint(acc / den));
+  }
+  consumer_sync(kConsumerThreads);
+}
+
 // Merge the split-KV partials of layer l into xin[Q] (every CTA, redundantly):
 // out = sum_j exp(m_j - M) acc_j / sum_j exp(m_j - M) l_j.
 // Each CTA polls every partial word exactly once per round: the per-head
 // (m, l) pairs by a few threads into shared memory, then each thread its EPT
 // accumulator words of every chunk (resolved together, one L2 round trip per
 // polling round).  Also writes the bf16 split terms of each output.
-template <class S>
+template <class S, bool M2>
 __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc) {
   constexpr int D = S::D, GRP = S::GRP;
+  if (M2 && nc >= kMerge2MinChunks) {
+    // Two-level: the per-head results are in the MH hop.
+    constexpr int EQ = (S::Q + kConsumerThreads - 1) / kConsumerThreads;
+    const uint64_t* mh = P.hop + HopLayout<S>::MH + (size_t)(l & 1) * S::Q;
+    uint64_t w[EQ];
+    const uint64_t* sp[EQ];
+#pragma unroll
+    for (int k = 0; k < EQ; ++k) {
+      sp[k] = mh + threadIdx.x + k * kConsumerThreads;
+      w[k] = threadIdx.x + k * kConsumerThreads < S::Q ? ld_relaxed(sp[k]) : 0;
+    }
+    const int nv = (S::Q - (int)threadIdx.x + kConsumerThreads - 1) / kConsumerThreads;
+    resolve_tagged<S, EQ>(P, sm, w, sp, nv < EQ ? nv : EQ, tag_of(seq, l, 1));
+#pragma unroll
+    for (int k = 0; k < EQ; ++k) {
+      const int i = threadIdx.x + k * kConsumerThreads;
+      if (i < S::Q) {
+        const float v = __uint_as_float((uint32_t)w[k]);
+        sm.xin[i] = v;
+        split_one(sm, i, v);
+      }
+    }
+    return;
+  }
   constexpr int EPT = S::Q >= kConsumerThreads ? S::Q / kConsumerThreads : 1;
   static_assert(D % EPT == 0, "a thread's outputs stay inside one head");
   const uint64_t* att = P.hop + HopLayout<S>::ATT + (size_t)(l & 1) * HopLayout<S>::kAttWords;
@@ -1225,7 +1334,7 @@ __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, u
   }
 }
 
-template <class S, int TP>
+template <class S, int TP, bool M2>
 __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const uint8_t* ring, int cta) {
   const int N = P.ncta, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Tensor parallelism (TP > 1): this GPU computes the MLP rows [rank IR,
@@ -1309,6 +1418,9 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
           kc += attention_item<S>(P, sm, ring, kc, t, l, p, seq, i / nc, i % nc, nc, i);
           appended |= (i % nc == nc - 1);
         }
+        if (M2 && nc >= kMerge2MinChunks)
+          for (int i = ilo; i < ihi; ++i)
+            if (i % nc == 0) merge_head<S>(P, sm, l, seq, nc, i / nc);
       }
       // ---- P3: merge -> O projection + residual --------------------------------
       {
@@ -1317,7 +1429,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         GemvPlan<S, S::Q, 2> gp;
         gp.prepare(P, sm, ring, kc, r1 - r0, 0, 0);
         MK_DP(8);
-        merge_attention<S>(P, sm, l, seq, nc);
+        merge_attention<S, M2>(P, sm, l, seq, nc);
         if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
         MK_DP(9);
         if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 3);
@@ -1523,7 +1635,11 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
   }
 }
 
-template <class S, int TP = 1>
+// M2: compile the two-level attention merge (used from kMerge2MinChunks chunks
+// per head on).  It is a separate instance because its code alone (about
+// 19 KB) slows the short-context steps that never use it: the kernel body
+// already exceeds the SM's instruction cache.
+template <class S, int TP = 1, bool M2 = false>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ KParams P) {
   static_assert(TP >= 1 && TP <= kMaxTP && S::I % TP == 0 && S::V % TP == 0 && (S::I / TP) % 16 == 0,
                 "tensor-parallel split");
@@ -1552,7 +1668,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     if (threadIdx.x < kConsumerThreads + 32) producer<S, TP>(sm.prm, sm, ring, cta);
   } else {
     setmaxnreg_inc<kConsumerRegs>();
-    consumers<S, TP>(sm.prm, sm, ring, cta);
+    consumers<S, TP, M2>(sm.prm, sm, ring, cta);
   }
 }
 

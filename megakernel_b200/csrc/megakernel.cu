@@ -38,7 +38,8 @@ struct State {
   bool capture_logits = false;
   size_t smem = 0;
   int vocab = 0;
-  const void* kernel = nullptr;
+  const void* kernel = nullptr;         // direct attention merge
+  const void* kernel_m2 = nullptr;      // two-level attention merge (long context)
 
   const __nv_bfloat16** d_wptr = nullptr;
   __nv_bfloat16* d_kv = nullptr;
@@ -72,7 +73,7 @@ void prefill_free(void* p);   // batch.cu
 }  // namespace
 
 namespace mk_tp {
-const void* kernel(int shape_id, int tp, size_t* hop_words);   // tp.cu
+const void* kernel(int shape_id, int tp, bool m2, size_t* hop_words);   // tp.cu
 }
 
 namespace {
@@ -235,11 +236,14 @@ int init_impl(void* d_weights, const long long* offsets, int num_offsets, const 
   }
   st->tp_rank = tp_rank;
   st->tp_size = tp_size;
-  if (tp_size > 1) {
+  {
     size_t words = 0;
-    st->kernel = mk_tp::kernel(id, tp_size, &words);
-    if (!st->kernel) return bail(MK_ERR_INVALID_ARG);   // (shape, TP size) not compiled
-    st->hop_bytes = words * 8;
+    st->kernel_m2 = mk_tp::kernel(id, tp_size, true, &words);
+    if (!st->kernel_m2) return bail(MK_ERR_INVALID_ARG);   // (shape, TP size) not compiled
+    if (tp_size > 1) {
+      st->kernel = st->kernel_m2;
+      st->hop_bytes = words * 8;
+    }
   }
   int sms = 0, coop = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
@@ -247,6 +251,8 @@ int init_impl(void* d_weights, const long long* offsets, int num_offsets, const 
     return bail(MK_ERR_CUDA);
   if (!coop) return bail(MK_ERR_LAUNCH);
   if (cudaFuncSetAttribute(st->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)st->smem) != cudaSuccess ||
+      cudaFuncSetAttribute(st->kernel_m2, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)st->smem) != cudaSuccess)
     return bail(MK_ERR_LAUNCH);
   int occ = 0;
@@ -342,7 +348,11 @@ int launch(State* st, const int* d_forced, int n_forced, int n_steps, int* d_out
   for (int j = 0; j < mk::kMaxTP; ++j) P.peer_hop[j] = st->peer_hop[j];
   MK_CUDA(cudaMemsetAsync(st->d_err, 0, sizeof(int), stream));
   void* args[] = {&P};
-  cudaError_t e = cudaLaunchCooperativeKernel(st->kernel, dim3(st->ncta), dim3(mk::kThreads), args,
+  // The two-level merge kernel once the launch reaches more chunks per head
+  // than the threshold at which that merge starts to pay (see shapes.cuh).
+  const int nc_last = mk::chunks_per_head<mk::ShapeD64>(st->pos + n_steps - 1);
+  const void* kern = nc_last > mk::kMerge2MinChunks ? st->kernel_m2 : st->kernel;
+  cudaError_t e = cudaLaunchCooperativeKernel(kern, dim3(st->ncta), dim3(mk::kThreads), args,
                                               st->smem, stream);
   if (e != cudaSuccess) {
     std::fprintf(stderr, "megakernel: launch failed: %s\n", cudaGetErrorString(e));

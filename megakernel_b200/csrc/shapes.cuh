@@ -25,13 +25,22 @@ constexpr int kMaxCtas = 256;
 constexpr int kRowsMax = 256;           // weight rows one CTA owns in one phase
 constexpr int kRowPad = 16;             // bytes between weight rows in a ring stage
 constexpr int kMaxTP = 8;               // tensor-parallel GPUs at most
+constexpr int kPvParts = 4;             // position parts of the attention P.V (warps / GRP)
 constexpr int kMaxChunksPerHead = 16;   // attention split-KV chunks per KV head
-// Fewest cached positions per chunk: below this a chunk's fixed costs (q/k/v
-// wait, QK-norm, RoPE, partial publish) outweigh the positions it walks.
+// Cached positions per split-KV chunk (at most): smaller chunks spread the
+// walk over more CTAs but cost more in the merge of their partials.
 #ifndef MK_CHUNK_MIN_POS
 #define MK_CHUNK_MIN_POS 128
 #endif
 constexpr int kChunkMinPos = MK_CHUNK_MIN_POS;
+// From this many chunks per head on, the partials are merged in two levels
+// (one CTA per KV head, then every CTA reads the merged heads).  Measured on
+// B200 (64-token launches): the extra exchange costs more than it saves up to
+// 4 chunks; at 5 chunks it wins, at 16 (p >= 1920) it saves ~150 us/token.
+#ifndef MK_MERGE2_MIN_CHUNKS
+#define MK_MERGE2_MIN_CHUNKS 5
+#endif
+constexpr int kMerge2MinChunks = MK_MERGE2_MIN_CHUNKS;
 
 template <int H_, int L_, int NQ_, int NKV_, int D_, int I_, int V_, int STB_>
 struct ShapeT {
@@ -49,8 +58,7 @@ struct ShapeT {
   static_assert(H % 256 == 0 && Q % 256 == 0 && I % 256 == 0, "K dims must be multiples of 256");
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(STB % 16 == 0 && NST >= 4, "ring");
-  static_assert(GRP * D * 4 == kConsumerThreads || GRP * D * 2 == kConsumerThreads ||
-                GRP * D == kConsumerThreads, "PV thread mapping");
+  static_assert(kPvParts * GRP == kConsumerWarps && GRP * D <= kConsumerThreads, "PV warp mapping");
 };
 
 // Shape 0: BASELINE configs[0] (head_dim 64, intermediate 2816).
