@@ -115,7 +115,9 @@ const char* megakernel_error_string(int code);
 int megakernel_set_trace(void* handle, void* d_buf, int steps);
 int megakernel_trace_points(void* handle);
 /* Profiling aid: sub-phase stamps of layer 1 into d_buf[steps][num_ctas][64]
- * (needs megakernel_set_trace active; NULL turns it off). */
+ * (needs megakernel_set_trace active; NULL turns it off).  Only in a library
+ * built with -DMK_DETAIL_STAMPS=1; otherwise a non-NULL d_buf returns
+ * MK_ERR_INVALID_ARG. */
 int megakernel_set_trace_detail(void* handle, void* d_buf);
 
 /* ---- decode without device allocation ------------------------------------ */

@@ -33,6 +33,20 @@
 // drops setmaxnreg when the kernel makes out-of-line calls.
 #define MK_PHASE __forceinline__
 
+// Sub-phase stamps of layer 1 (megakernel_set_trace_detail): a profiling
+// build only (-DMK_DETAIL_STAMPS=1), since they add 6 KB to the kernel body.
+#ifndef MK_DETAIL_STAMPS
+#define MK_DETAIL_STAMPS 0
+#endif
+// Coarse per-phase trace stamps (megakernel_set_trace).
+#ifndef MK_TRACE_POINTS
+#define MK_TRACE_POINTS 1
+#endif
+// Measurement only: drop the re-poll loops of tagged waits.
+#ifndef MK_DBG_NOSLOW
+#define MK_DBG_NOSLOW 0
+#endif
+
 // Unroll factor of the GEMV's streamed-slice loop: more ldmatrix loads in
 // flight per warp (measured on B200: 1 -> +8 % per token, 2 -> 4 -> 8 each
 // about -1.5 %; the code grows by under 1 KB).
@@ -131,17 +145,22 @@ struct Trace {
 
 template <class S>
 __device__ __forceinline__ void trace_point(const KParams& P, int t, int cta, int k) {
-  if (P.trace != nullptr && t < P.trace_steps)
+  if (MK_TRACE_POINTS && P.trace != nullptr && t < P.trace_steps)
     P.trace[((size_t)t * P.ncta + cta) * Trace<S>::kPoints + k] = globaltimer_ns();
 }
 
 // Sub-phase stamp k of layer 1 (profiling aid; off unless P.detail is set).
+
+#if MK_DETAIL_STAMPS
 #define MK_DP(k)                                                                      \
   do {                                                                                \
     if (P.detail != nullptr && l == 1 && t < P.trace_steps &&                         \
         (threadIdx.x == 0 || threadIdx.x == kConsumerThreads))                        \
       P.detail[((size_t)t * P.ncta + blockIdx.x) * 64 + (k)] = globaltimer_ns();      \
   } while (0)
+#else
+#define MK_DP(k) do {} while (0)
+#endif
 
 template <class S>
 struct Smem {
@@ -437,6 +456,9 @@ __device__ __forceinline__ void resolve_tagged(const KParams& P, Smem<S>& sm, ui
   for (int k = 0; k < NB; ++k) miss |= (k < nvalid) && (uint32_t)(w[k] >> 32) != tag;
   if (!miss) return;
   Spin sp;
+#if MK_DBG_NOSLOW
+  if (false)
+#endif
   while (miss && sp.keep_going(P, sm)) {
     // Back off between rounds: every CTA polls the same words, and re-issuing
     // all of them back to back floods the L2 slices that hold them (the
@@ -1106,27 +1128,34 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
   for (int k = 0; k < D / 32; ++k) acc[k] = 0.f;
   // Positions held outside the ring -- p-1 (slot 0) and the current p (slot
   // 1) -- ride along with the first ring block (or form the only block).
+  // Cached positions [c0, te) stream through the ring as (K, V) stage pairs.
+  // One call site for attend_block: it is inlined, and a second site would
+  // add ~10 KB to a kernel body that already overflows the instruction cache.
   const int s0 = prev ? 0 : 1;
   int ne = (prev ? 1 : 0) + (last ? 1 : 0);
-  if (c0 >= te && ne > 0) attend_block(sm, &sm.kx[s0][0], &sm.vx[s0][0], ne, &sm.kx[0][0], &sm.vx[0][0], 0, acc);
-  // Cached positions [c0, te) streamed through the ring as (K, V) stage pairs.
-  for (int a = c0; a < te; a += S::SUBP) {
-    const int n = min(S::SUBP, te - a);
+  for (int a = c0, first = 1; first || a < te; a += S::SUBP, first = 0) {
+    const bool ring_blk = a < te;
+    const int n = ring_blk ? min(S::SUBP, te - a) : 0;
     const uint32_t sk = kc % nst, pk = (kc / nst) & 1u;
     const uint32_t sv = (kc + 1) % nst, pv = ((kc + 1) / nst) & 1u;
-    const bool okk = wait_bar(P, sm, &sm.full[sk], pk);
-    const bool okv = okk && wait_bar(P, sm, &sm.full[sv], pv);
+    bool ok = true;
+    if (ring_blk) {
+      ok = wait_bar(P, sm, &sm.full[sk], pk);
+      ok = ok && wait_bar(P, sm, &sm.full[sv], pv);
+    }
     const int blk = (a - c0) / S::SUBP;
     if (blk < 4) MK_DP(20 + 2 * blk);
-    if (!consumer_any(kConsumerThreads, !(okk && okv))) {
+    if (!consumer_any(kConsumerThreads, !ok) && n + ne > 0) {
       attend_block(sm, reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sk * S::STB),
                    reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)sv * S::STB), n,
                    &sm.kx[s0][0], &sm.vx[s0][0], ne, acc);
     }
     if (blk < 4) MK_DP(21 + 2 * blk);
     ne = 0;
-    if (lane == 0) { mbar_arrive(&sm.empty[sk]); mbar_arrive(&sm.empty[sv]); }
-    kc += 2;
+    if (ring_blk) {
+      if (lane == 0) { mbar_arrive(&sm.empty[sk]); mbar_arrive(&sm.empty[sv]); }
+      kc += 2;
+    }
   }
   MK_DP(7);
   {

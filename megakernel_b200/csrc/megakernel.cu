@@ -637,6 +637,9 @@ int megakernel_trace_points(void* handle) {
 int megakernel_set_trace_detail(void* handle, void* d_buf) {
   State* st = as_state(handle);
   if (!st) return MK_ERR_INVALID_ARG;
+  // The sub-phase stamps are compiled in only with -DMK_DETAIL_STAMPS=1 (they
+  // cost 6 KB of instruction-cache-bound kernel code).
+  if (!MK_DETAIL_STAMPS && d_buf != nullptr) return MK_ERR_INVALID_ARG;
   st->d_detail = static_cast<uint64_t*>(d_buf);
   return MK_OK;
 }
