@@ -111,7 +111,10 @@ const char* megakernel_error_string(int code);
  * 3 attention merged, 4 x after attention published, 5 MLP hidden published,
  * 6 layer output published; then 7L lm-head start, 7L+1 lm partial published,
  * 7L+2 next token known, 7L+3 ns spent waiting on activation hops (thread 0),
- * 7L+4 SM clock cycles over the step.  steps = 0 turns tracing off. */
+ * 7L+4 SM clock cycles over the step.  steps = 0 turns tracing off.
+ * Profiling builds only (-DMK_TRACE_POINTS=1): the stamps are kernel code,
+ * and this kernel is bound by its instruction-cache footprint; a default
+ * build returns MK_ERR_INVALID_ARG for steps > 0. */
 int megakernel_set_trace(void* handle, void* d_buf, int steps);
 int megakernel_trace_points(void* handle);
 /* Profiling aid: sub-phase stamps of layer 1 into d_buf[steps][num_ctas][64]

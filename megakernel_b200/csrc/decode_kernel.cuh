@@ -32,15 +32,19 @@
 // warpgroups run with different register budgets (setmaxnreg), and ptxas
 // drops setmaxnreg when the kernel makes out-of-line calls.
 #define MK_PHASE __forceinline__
+#ifndef MK_DBG_SPIN
+#define MK_DBG_SPIN 0
+#endif
 
 // Sub-phase stamps of layer 1 (megakernel_set_trace_detail): a profiling
 // build only (-DMK_DETAIL_STAMPS=1), since they add 6 KB to the kernel body.
 #ifndef MK_DETAIL_STAMPS
 #define MK_DETAIL_STAMPS 0
 #endif
-// Coarse per-phase trace stamps (megakernel_set_trace).
+// Coarse per-phase trace stamps (megakernel_set_trace): also a profiling
+// build only (-DMK_TRACE_POINTS=1, 4 KB of kernel code).
 #ifndef MK_TRACE_POINTS
-#define MK_TRACE_POINTS 1
+#define MK_TRACE_POINTS 0
 #endif
 // Measurement only: drop the re-poll loops of tagged waits.
 #ifndef MK_DBG_NOSLOW
@@ -144,7 +148,10 @@ struct Trace {
 };
 
 template <class S>
-__device__ __forceinline__ void trace_point(const KParams& P, int t, int cta, int k) {
+struct Smem;
+template <class S>
+__device__ __forceinline__ void trace_point(const KParams& P, Smem<S>& sm, int t, int cta, int k) {
+  sm.progress = sm.progress + 1u;   // watchdog: this CTA is advancing
   if (MK_TRACE_POINTS && P.trace != nullptr && t < P.trace_steps)
     P.trace[((size_t)t * P.ncta + cta) * Trace<S>::kPoints + k] = globaltimer_ns();
 }
@@ -187,6 +194,8 @@ struct Smem {
   int next_token;
   volatile int abort_flag;
   volatile int tokens_done;
+  volatile uint32_t progress;         // bumped at every phase (watchdog)
+  volatile int done;                  // consumers finished (watchdog exits)
   unsigned long long wait_hop_ns;     // trace accounting (thread 0)
   const __nv_bfloat16* wtab[S::NOFF]; // weight pointer table (offsets order)
   KParams prm;                        // copy of the launch parameters
@@ -202,22 +211,17 @@ __device__ __forceinline__ void fail(const KParams& P, Smem<S>& sm, int code) {
   sm.abort_flag = 1;
 }
 
-// Bounded spin helper: returns false when the wait must be abandoned
-// (deadline passed, this CTA aborted, or another CTA reported an error).
+// Spin helper of every wait: returns false when the wait must be abandoned
+// (this CTA aborted).  Waits are bounded by the CTA's watchdog warp
+// (decode_kernel), which raises abort_flag when the CTA has made no progress
+// for timeout_ns or another CTA has reported an error; each wait site only
+// reads the flag, which keeps the (inlined, instruction-cache-bound) wait
+// code small.
 struct Spin {
-  uint64_t t0 = 0;
-  uint32_t it = 0;
   template <class S>
   __device__ __forceinline__ bool keep_going(const KParams& P, Smem<S>& sm) {
-    if (sm.abort_flag) return false;
-    if ((++it & 63u) == 0) {
-      uint64_t now = globaltimer_ns();
-      if (t0 == 0) t0 = now;
-      else if ((long long)(now - t0) > P.timeout_ns) { fail(P, sm, MK_ERR_TIMEOUT); return false; }
-      // Another CTA's failure: checked rarely, every spinner reads this word.
-      if ((it & 4095u) == 0 && ld_volatile_i32(P.err) != 0) { sm.abort_flag = 1; return false; }
-    }
-    return true;
+    (void)P;
+    return !sm.abort_flag;
   }
 };
 
@@ -409,7 +413,7 @@ __device__ __forceinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t*
     const int nitems = S::NKV * nc;
 #pragma unroll 1
     for (int l = 0; l < S::L && pr.ok; ++l) {
-      trace_point<S>(P, t, cta, 7 * l);
+      trace_point<S>(P, sm, t, cta, 7 * l);
       int r0, r1;
       split_rows(S::QKV, N, cta, phase_rot(l, 0, N), r0, r1);
 #pragma unroll 1
@@ -483,7 +487,7 @@ template <class S>
 __device__ MK_PHASE void wait_tagged(const KParams& P, Smem<S>& sm, const uint64_t* src,
                                             int n, uint32_t tag, float* dst) {
   constexpr int kBatch = 12;
-  const uint64_t tw0 = (P.trace != nullptr && threadIdx.x == 0) ? globaltimer_ns() : 0;
+  const uint64_t tw0 = (MK_TRACE_POINTS && P.trace != nullptr && threadIdx.x == 0) ? globaltimer_ns() : 0;
   for (int base = threadIdx.x; base < n; base += kConsumerThreads * kBatch) {
     uint64_t v[kBatch];
 #pragma unroll
@@ -1298,11 +1302,12 @@ __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, u
   const bool active = e0 < S::Q;
   const int qh = active ? e0 / D : 0, d0 = e0 % D, g = qh % GRP;
   const uint64_t* b = att + ((size_t)(qh / GRP) * nc * GRP + g) * (D + 2) + d0;
-  // Accumulator words, kGroup chunks at a time (registers bound the group):
-  // the first group's loads are issued before the (m, l) sync, so with
-  // nc <= kGroup the merge costs one polling round trip.  Word q of a group
+  // Accumulator words, kGroup chunks at a time (registers and code size bound
+  // the group; from kMerge2MinChunks chunks on the two-level merge runs
+  // instead, so one group covers every direct merge of a launch that picks
+  // its kernel by position).  Word q of a group
   // is chunk j0 + q / EPT, element q % EPT.
-  constexpr int kGroup = 8, NW = kGroup * EPT;
+  constexpr int kGroup = kMerge2MinChunks, NW = kGroup * EPT;
   uint64_t w[NW];
 #if MK_MERGE_ML_FIRST
   // Poll the accumulator words only once every (m, l) pair is present: their
@@ -1426,7 +1431,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         }
         norm_partial(sm, ss);
         if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
-        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 1);
+        if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 1);
         MK_DP(1);
         kc += gp.finish(P, sm, sm.rowsum[0] + oq[0], sm.rowsum[0] + oq[1], sm.rowsum[0] + oq[2], true);
       }
@@ -1437,7 +1442,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         for (int r = tid; r < s1 - s0; r += kConsumerThreads)
           st_tagged(dst + s0 + r, tg, __float_as_uint(sm.rowsum[0][r]));
         // (no barrier needed: the next writer of rowsum[0] is behind several)
-        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 2);
+        if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 2);
       }
       // ---- P2: attention items owned by this CTA ------------------------------
       {
@@ -1461,14 +1466,14 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         merge_attention<S, M2>(P, sm, l, seq, nc);
         if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
         MK_DP(9);
-        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 3);
+        if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 3);
         kc += gp.finish(P, sm, sm.rowsum[0], nullptr, nullptr, false);
         MK_DP(10);
         uint64_t* dst = P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H;
         const uint32_t tg = tag_of(seq, l, 2);
         for (int r = tid; r < r1 - r0; r += kConsumerThreads)
           st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
-        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 4);
+        if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 4);
       }
       // ---- P4: x' -> RMSNorm -> silu(gate) * up ---------------------------------
       {
@@ -1495,7 +1500,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
           const float hval = (g / (1.0f + expf(-g))) * u;
           st_tagged(dst + r0 + r, tg, __float_as_uint(hval));
         }
-        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 5);
+        if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 5);
       }
       // ---- P5: h -> down projection + residual --------------------------------
       {
@@ -1529,7 +1534,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         }
         // xres is rewritten by the next layer's hop: finish the reads first.
         consumer_sync(kConsumerThreads);
-        if (tid == 0) trace_point<S>(P, t, cta, 7 * l + 6);
+        if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 6);
       }
     }
     // ---- final RMSNorm -> LM head -> argmax ------------------------------------
@@ -1551,7 +1556,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
                                   tag_of(seq, S::L - 1, 4), fgains);
     if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
     rmsnorm_to_xin(sm, fgains);
-    if (tid == 0) trace_point<S>(P, t, cta, 7 * S::L);
+    if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * S::L);
     {
       int r0, r1;
       split_rows(VR, N, cta, phase_rot(S::L, 4, N), r0, r1);
@@ -1583,7 +1588,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
             st_tagged_sys(P.peer_hop[j] + lm_off + 2 * slot + 1, tg, (uint32_t)ix);
           }
         }
-        trace_point<S>(P, t, cta, 7 * S::L + 1);
+        trace_point<S>(P, sm, t, cta, 7 * S::L + 1);
       }
       // Every CTA reduces all CTAs' (max, index) pairs: lowest index wins ties.
       if constexpr (TP == 1) {
@@ -1650,8 +1655,8 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
       tok = (t + 1 < P.n_forced) ? P.forced[t + 1] : best;
       if (tok < 0 || tok >= S::V) tok = 0;  // forced ids are range-checked on the host
       if (tid == 0) {
-        trace_point<S>(P, t, cta, 7 * S::L + 2);
-        if (P.trace != nullptr && t < P.trace_steps) {
+        trace_point<S>(P, sm, t, cta, 7 * S::L + 2);
+        if (MK_TRACE_POINTS && P.trace != nullptr && t < P.trace_steps) {
           uint64_t* tr = P.trace + ((size_t)t * P.ncta + cta) * Trace<S>::kPoints;
           tr[7 * S::L + 3] = sm.wait_hop_ns;
           tr[7 * S::L + 4] = (uint64_t)(clock64() - clk0);
@@ -1660,6 +1665,33 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         __threadfence();
         sm.tokens_done = t + 1;
       }
+    }
+  }
+}
+
+// Watchdog (one thread of the producer warpgroup): every wait in this CTA is
+// bounded through it.  It records an error and raises abort_flag when the
+// CTA's progress counter has not moved for timeout_ns (MK_ERR_TIMEOUT) or
+// when another CTA has reported an error; every wait then gives up, the
+// roles leave at their next barrier, and the producer drains its copies.
+template <class S>
+__device__ __forceinline__ void watchdog(const KParams& P, Smem<S>& sm) {
+  uint32_t last = sm.progress;
+  uint64_t t_last = globaltimer_ns();
+  while (!sm.done && !sm.abort_flag) {
+    __nanosleep(500);
+    const uint64_t now = globaltimer_ns();
+    const uint32_t pr = sm.progress;
+    if (pr != last) {
+      last = pr;
+      t_last = now;
+    } else if ((long long)(now - t_last) > P.timeout_ns) {
+      fail(P, sm, MK_ERR_TIMEOUT);
+      break;
+    }
+    if (ld_volatile_i32(P.err) != 0) {
+      sm.abort_flag = 1;
+      break;
     }
   }
 }
@@ -1684,6 +1716,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     sm.abort_flag = 0;
     sm.tokens_done = 0;
+    sm.progress = 0;
+    sm.done = 0;
     sm.wait_hop_ns = 0;
     fence_mbar_init();
   }
@@ -1695,9 +1729,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   if (threadIdx.x >= kConsumerThreads) {
     setmaxnreg_dec<kProducerRegs>();
     if (threadIdx.x < kConsumerThreads + 32) producer<S, TP>(sm.prm, sm, ring, cta);
+    else if (threadIdx.x == kConsumerThreads + 32) watchdog<S>(sm.prm, sm);
   } else {
     setmaxnreg_inc<kConsumerRegs>();
     consumers<S, TP, M2>(sm.prm, sm, ring, cta);
+    if (threadIdx.x == 0) sm.done = 1;
   }
 }
 

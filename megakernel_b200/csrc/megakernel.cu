@@ -619,6 +619,8 @@ const char* megakernel_error_string(int code) {
 int megakernel_set_trace(void* handle, void* d_buf, int steps) {
   State* st = as_state(handle);
   if (!st || steps < 0 || (steps > 0 && !d_buf)) return MK_ERR_INVALID_ARG;
+  // Compiled in only with -DMK_TRACE_POINTS=1 (profiling builds).
+  if (!MK_TRACE_POINTS && steps > 0) return MK_ERR_INVALID_ARG;
   st->d_trace = steps > 0 ? static_cast<uint64_t*>(d_buf) : nullptr;
   st->trace_steps = steps;
   return MK_OK;
