@@ -32,9 +32,6 @@
 // warpgroups run with different register budgets (setmaxnreg), and ptxas
 // drops setmaxnreg when the kernel makes out-of-line calls.
 #define MK_PHASE __forceinline__
-#ifndef MK_DBG_SPIN
-#define MK_DBG_SPIN 0
-#endif
 
 // Sub-phase stamps of layer 1 (megakernel_set_trace_detail): a profiling
 // build only (-DMK_DETAIL_STAMPS=1), since they add 6 KB to the kernel body.
@@ -46,10 +43,6 @@
 #ifndef MK_TRACE_POINTS
 #define MK_TRACE_POINTS 0
 #endif
-// Measurement only: drop the re-poll loops of tagged waits.
-#ifndef MK_DBG_NOSLOW
-#define MK_DBG_NOSLOW 0
-#endif
 
 // Unroll factor of the GEMV's streamed-slice loop: more ldmatrix loads in
 // flight per warp (measured on B200: 1 -> +8 % per token, 2 -> 4 -> 8 each
@@ -57,12 +50,13 @@
 #ifndef MK_GEMV_UNROLL
 #define MK_GEMV_UNROLL 8
 #endif
+// Unroll of the attention P.V position loop (code size vs load overlap).
+#ifndef MK_PV_UNROLL
+#define MK_PV_UNROLL 4
+#endif
 // Weight slices per tile loaded into registers before the GEMV input arrives.
 #ifndef MK_GEMV_PIT
 #define MK_GEMV_PIT 2
-#endif
-#ifndef MK_DBG_ATT
-#define MK_DBG_ATT 0
 #endif
 // Pause between polling rounds of a tagged-word wait (ns).
 #ifndef MK_POLL_BACKOFF_NS
@@ -72,6 +66,7 @@
 namespace mk {
 
 constexpr int kGemvUnroll = MK_GEMV_UNROLL;
+constexpr int kPvUnroll = MK_PV_UNROLL;
 
 enum : int {
   MK_OK = 0,
@@ -460,9 +455,6 @@ __device__ __forceinline__ void resolve_tagged(const KParams& P, Smem<S>& sm, ui
   for (int k = 0; k < NB; ++k) miss |= (k < nvalid) && (uint32_t)(w[k] >> 32) != tag;
   if (!miss) return;
   Spin sp;
-#if MK_DBG_NOSLOW
-  if (false)
-#endif
   while (miss && sp.keep_going(P, sm)) {
     // Back off between rounds: every CTA polls the same words, and re-issuing
     // all of them back to back floods the L2 slices that hold them (the
@@ -925,10 +917,7 @@ __device__ MK_PHASE void attend_block(Smem<S>& sm, const __nv_bfloat16* K1, cons
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = n1 + n2;
   const float scale = (D == 64) ? 0.125f : 0.08838834764831845f;  // D^-0.5
-#if MK_DBG_ATT == 1
-  for (int i = threadIdx.x; i < GRP * n; i += kConsumerThreads) sm.sc[i / n][i % n] = 0.f;
-  if (false)
-#endif
+#pragma unroll 1
   for (int i = threadIdx.x; i < GRP * n; i += kConsumerThreads) {
     const int g = i / n, pos = i - g * n;
     const __nv_bfloat16* kr = pos < n1 ? K1 + (size_t)pos * D : K2 + (size_t)(pos - n1) * D;
@@ -952,19 +941,17 @@ __device__ MK_PHASE void attend_block(Smem<S>& sm, const __nv_bfloat16* K1, cons
     sm.sc[g][pos] = (s0 + s1) * scale;
   }
   consumer_sync(kConsumerThreads);
-#if MK_DBG_ATT == 2
-  if (warp < GRP && lane == 0) { sm.corr[warp] = 1.f; }
-  if (false)
-#endif
   if (warp < GRP) {
     const int g = warp;
     float mx = -INFINITY;
+#pragma unroll 1
     for (int pos = lane; pos < n; pos += 32) mx = fmaxf(mx, sm.sc[g][pos]);
     mx = warp_max(mx);
     const float mold = sm.mrun[g];
     const float mnew = fmaxf(mold, mx);
     const float c = expf(mold - mnew);
     float sum = 0.f;
+#pragma unroll 1
     for (int pos = lane; pos < n; pos += 32) {
       const float e = expf(sm.sc[g][pos] - mnew);
       sm.sc[g][pos] = e;
@@ -997,10 +984,7 @@ __device__ MK_PHASE void attend_block(Smem<S>& sm, const __nv_bfloat16* K1, cons
       }
     };
     int pos = part;
-#if MK_DBG_ATT == 3
-    pos = n;
-#endif
-#pragma unroll 4
+#pragma unroll kPvUnroll
     for (; pos + kPvParts < n1; pos += 2 * kPvParts) {
       fma_row(a, sm.sc[g][pos], V1 + (size_t)pos * D);
       fma_row(b, sm.sc[g][pos + kPvParts], V1 + (size_t)(pos + kPvParts) * D);
