@@ -38,11 +38,11 @@ METRIC = "decode tok/s, Qwen3-0.6B shape, B=1 on 1×B200; % of HBM roofline"
 PROMPT, GEN = 128, 512
 # Measured DRAM traffic of the decode kernel relative to its algorithmic bytes,
 # from the ncu capture summarised in profiles/decode_kernel_d64_b1.md (one
-# launch of 2 tokens at positions 128-129: 1.958796 GB read + 3.49696 MB
+# launch of 2 tokens at positions 128-129: 1.958453 GB read + 4.3072 MB
 # written against 979,346,432 + 979,403,776 algorithmic bytes).  The launch's traffic is
 # scaled from it by the algorithmic bytes of the timed launch (traffic grows
 # with the K/V bytes the same way).
-NCU_TRAFFIC_RATIO = (1_958_796_000 + 3_496_960) / (979_346_432 + 979_403_776)
+NCU_TRAFFIC_RATIO = (1_958_453_000 + 4_307_200) / (979_346_432 + 979_403_776)
 
 
 def load_peaks():
