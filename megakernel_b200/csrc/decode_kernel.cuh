@@ -22,8 +22,9 @@
 // the (step, layer, phase), so a reader spins on the words it needs until the
 // tags match: no counters, no grid barriers, no fences on the critical path.
 // The reference instead runs 144 atomic grid barriers per token
-// (src/barriers.cuh:38-73).  Every wait is bounded by a globaltimer deadline;
-// on expiry the CTA records an error code and all roles exit.
+// (src/barriers.cuh:38-73).  Every wait is bounded through a per-CTA watchdog
+// thread (no progress for timeout_ns, or another CTA's error, raises the
+// CTA's abort flag); the CTA then records an error code and all roles exit.
 #pragma once
 #include "ptx.cuh"
 #include "shapes.cuh"
