@@ -100,6 +100,14 @@ int megakernel_max_seq(void* handle);
 int megakernel_shape_id(void* handle);
 int megakernel_num_ctas(void* handle);
 
+/* Attention-merge kernel choice for later launches: 0 (default) picks the
+ * two-level merge once a launch reaches MK_MERGE2_MIN_CHUNKS (5) split-KV
+ * chunks per head (positions > 512) and the direct merge before; 1 always
+ * the direct merge; 2 always the kernel instance that carries the two-level
+ * merge (it still merges directly below 5 chunks).  Results agree within
+ * fp32 rounding; the choice only changes speed.  No reference counterpart. */
+int megakernel_set_merge_mode(void* handle, int mode);
+
 /* Last error of this handle (MK_OK if none) and a description of a code. */
 int megakernel_last_error(void* handle);
 const char* megakernel_error_string(int code);
@@ -142,7 +150,11 @@ int megakernel_set_trace_detail(void* handle, void* d_buf);
  * on a device (the current one) sets that device up with blocking copies:
  * make it before any stream capture.  All calls share the scratch, so calls
  * that overlap on the GPU race.  Blocks until done; returns MK_OK or an
- * MK_ERR_* code.  The caller tracks the position (pos += n_steps). */
+ * MK_ERR_* code.  The caller tracks the position (pos += n_steps).
+ * d_weights and d_kv must be 16-byte aligned (MK_ERR_INVALID_ARG otherwise);
+ * a forced token id outside the vocabulary returns MK_ERR_INVALID_ARG.  Like
+ * megakernel_decode_n it runs the kernel instance with the two-level
+ * attention merge once pos + n_steps - 1 reaches 5 chunks per head (> 512). */
 int megakernel_decode_noalloc(const void* d_weights, const long long* offsets, int num_offsets,
                               void* d_kv, int kv_max_seq, int pos, const int* d_tokens,
                               int n_forced, int n_steps, int* d_out, float* d_logits,

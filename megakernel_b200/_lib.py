@@ -100,6 +100,7 @@ def signatures() -> dict:
         "megakernel_max_seq": ([vp], c_int),
         "megakernel_shape_id": ([vp], c_int),
         "megakernel_num_ctas": ([vp], c_int),
+        "megakernel_set_merge_mode": ([vp, c_int], c_int),
         "megakernel_last_error": ([vp], c_int),
         "megakernel_error_string": ([c_int], ctypes.c_char_p),
         "megakernel_set_trace": ([vp, vp, c_int], c_int),

@@ -237,6 +237,10 @@ class MegakernelEngine:
         buf = ctypes.create_string_buffer(b"".join(handles), 64 * self.tp_size)
         _lib.check(self.lib.megakernel_tp_connect(self._handle, buf), "megakernel_tp_connect")
 
+    def set_merge_mode(self, mode: int):
+        """0 auto (default), 1 direct attention merge, 2 two-level merge instance."""
+        _lib.check(self.lib.megakernel_set_merge_mode(self._handle, int(mode)), "megakernel_set_merge_mode")
+
     def set_logits_capture(self, enable=True):
         _lib.check(self.lib.megakernel_set_logits_capture(self._handle, int(enable)))
 

@@ -1190,7 +1190,7 @@ __device__ MK_PHASE uint32_t attention_item(const KParams& P, Smem<S>& sm, const
 // every partial (at 16 chunks the direct merge had each of 148 CTAs read
 // 135 KB of partials, about 9 us per layer).  Called after all of this CTA's
 // items of the layer, so it never waits on a partial this CTA has yet to make.
-template <class S>
+template <class S, int TP>
 __device__ MK_PHASE void merge_head(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc, int h) {
   constexpr int D = S::D, GRP = S::GRP;
   static_assert(GRP * kMaxChunksPerHead <= kConsumerThreads && GRP * D <= kConsumerThreads, "merge_head");
@@ -1229,7 +1229,7 @@ __device__ MK_PHASE void merge_head(const KParams& P, Smem<S>& sm, int l, uint32
         acc = fmaf(__uint_as_float((uint32_t)w[j]), cj, acc);
       }
     }
-    st_tagged(P.hop + HopLayout<S>::MH + (size_t)(l & 1) * S::Q + (size_t)(h * GRP + g) * D + dd, ta,
+    st_tagged(P.hop + HopLayout<S, TP>::MH + (size_t)(l & 1) * S::Q + (size_t)(h * GRP + g) * D + dd, ta,
               __float_as_uint(acc / den));
   }
   consumer_sync(kConsumerThreads);
@@ -1241,13 +1241,13 @@ __device__ MK_PHASE void merge_head(const KParams& P, Smem<S>& sm, int l, uint32
 // (m, l) pairs by a few threads into shared memory, then each thread its EPT
 // accumulator words of every chunk (resolved together, one L2 round trip per
 // polling round).  Also writes the bf16 split terms of each output.
-template <class S, bool M2>
+template <class S, int TP, bool M2>
 __device__ MK_PHASE void merge_attention(const KParams& P, Smem<S>& sm, int l, uint32_t seq, int nc) {
   constexpr int D = S::D, GRP = S::GRP;
   if (M2 && nc >= kMerge2MinChunks) {
     // Two-level: the per-head results are in the MH hop.
     constexpr int EQ = (S::Q + kConsumerThreads - 1) / kConsumerThreads;
-    const uint64_t* mh = P.hop + HopLayout<S>::MH + (size_t)(l & 1) * S::Q;
+    const uint64_t* mh = P.hop + HopLayout<S, TP>::MH + (size_t)(l & 1) * S::Q;
     uint64_t w[EQ];
     const uint64_t* sp[EQ];
 #pragma unroll
@@ -1371,6 +1371,14 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
     const int nitems = S::NKV * nc;
     const long long clk0 = clock64();
     bool appended = false;
+    // Token ids come from the caller (forced) or from the argmax below; a
+    // forced id outside the vocabulary ends the launch with
+    // MK_ERR_INVALID_ARG before its embedding row is read (every CTA sees
+    // the same id and leaves here).
+    if (tok < 0 || tok >= S::V) {
+      if (tid == 0) fail(P, sm, MK_ERR_INVALID_ARG);
+      return;
+    }
     {
       const __nv_bfloat16* er = sm.wtab[0] + (size_t)tok * S::H;
       for (int i = tid; i < S::H; i += kConsumerThreads) sm.xres[i] = __bfloat162float(er[i]);
@@ -1439,7 +1447,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         }
         if (M2 && nc >= kMerge2MinChunks)
           for (int i = ilo; i < ihi; ++i)
-            if (i % nc == 0) merge_head<S>(P, sm, l, seq, nc, i / nc);
+            if (i % nc == 0) merge_head<S, TP>(P, sm, l, seq, nc, i / nc);
       }
       // ---- P3: merge -> O projection + residual --------------------------------
       {
@@ -1448,7 +1456,7 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         GemvPlan<S, S::Q, 2> gp;
         gp.prepare(P, sm, ring, kc, r1 - r0, 0, 0);
         MK_DP(8);
-        merge_attention<S, M2>(P, sm, l, seq, nc);
+        merge_attention<S, TP, M2>(P, sm, l, seq, nc);
         if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
         MK_DP(9);
         if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 3);
@@ -1638,7 +1646,6 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
       const int best = sm.next_token;
       if (cta == 0 && tid == 0) P.out_tokens[t] = best;
       tok = (t + 1 < P.n_forced) ? P.forced[t + 1] : best;
-      if (tok < 0 || tok >= S::V) tok = 0;  // forced ids are range-checked on the host
       if (tid == 0) {
         trace_point<S>(P, sm, t, cta, 7 * S::L + 2);
         if (MK_TRACE_POINTS && P.trace != nullptr && t < P.trace_steps) {

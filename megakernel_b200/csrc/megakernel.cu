@@ -36,6 +36,7 @@ struct State {
   long long timeout_ns = 1000000000LL;
   int debug_skip_cta = -1;
   bool capture_logits = false;
+  int merge_mode = 0;           // 0 auto, 1 direct, 2 two-level instance
   size_t smem = 0;
   int vocab = 0;
   const void* kernel = nullptr;         // direct attention merge
@@ -351,7 +352,8 @@ int launch(State* st, const int* d_forced, int n_forced, int n_steps, int* d_out
   // The two-level merge kernel once the launch reaches more chunks per head
   // than the threshold at which that merge starts to pay (see shapes.cuh).
   const int nc_last = mk::chunks_per_head<mk::ShapeD64>(st->pos + n_steps - 1);
-  const void* kern = nc_last > mk::kMerge2MinChunks ? st->kernel_m2 : st->kernel;
+  const bool m2 = st->merge_mode == 2 || (st->merge_mode == 0 && nc_last >= mk::kMerge2MinChunks);
+  const void* kern = m2 ? st->kernel_m2 : st->kernel;
   cudaError_t e = cudaLaunchCooperativeKernel(kern, dim3(st->ncta), dim3(mk::kThreads), args,
                                               st->smem, stream);
   if (e != cudaSuccess) {
@@ -597,6 +599,15 @@ int megakernel_num_ctas(void* handle) {
   State* st = as_state(handle);
   return st ? st->ncta : -1;
 }
+int megakernel_set_merge_mode(void* handle, int mode) {
+  State* st = as_state(handle);
+  if (!st || mode < 0 || mode > 2) return MK_ERR_INVALID_ARG;
+  // Tensor-parallel engines run only the instance with the two-level merge.
+  if (st->tp_size > 1 && mode == 1) return set_err(st, MK_ERR_INVALID_ARG);
+  st->merge_mode = mode;
+  return MK_OK;
+}
+
 int megakernel_last_error(void* handle) {
   State* st = as_state(handle);
   return st ? st->last_error : MK_ERR_INVALID_ARG;

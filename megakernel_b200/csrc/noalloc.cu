@@ -51,6 +51,7 @@ struct DeviceSetup {
   bool done = false;
   unsigned char* base = nullptr;  // device address of g_scratch on this device
   int sms = 0;
+  const void* kernel_m2 = nullptr;
 };
 DeviceSetup g_setup[kMaxDevices];
 std::mutex g_mutex;
@@ -71,22 +72,25 @@ int setup_device(int dev, DeviceSetup** out) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)mk::smem_bytes<SNA>()) != cudaSuccess)
       return MK_ERR_LAUNCH;
-    // RoPE tables (same formula as the allocating path), staged through a
-    // fixed host buffer and copied with blocking copies.
-    static float table[kMaxPos * (SNA::D / 2)];
-    const int half = SNA::D / 2;
-    for (int which = 0; which < 2; ++which) {
-      for (int i = 0; i < half; ++i) {
-        const float expo = (float)(2 * i) / (float)SNA::D;
-        const float inv = 1.0f / (float)pow(1.0e6, (double)expo);
-        for (int q = 0; q < kMaxPos; ++q) {
-          const double ang = (double)((float)q * inv);
-          table[(size_t)q * half + i] = which == 0 ? (float)cos(ang) : (float)sin(ang);
-        }
-      }
-      unsigned char* dst = static_cast<unsigned char*>(p) + (which == 0 ? kCosOff : kSinOff);
-      if (cudaMemcpy(dst, table, kRopeBytes, cudaMemcpyHostToDevice) != cudaSuccess) return MK_ERR_CUDA;
-    }
+    // The two-level-merge instance (compiled in tp.cu), used once a call
+    // reaches kMerge2MinChunks chunks per head, as the allocating path does.
+    size_t words = 0;
+    s.kernel_m2 = mk_tp::kernel(0, 1, true, &words);
+    if (!s.kernel_m2 || words * sizeof(uint64_t) != kHopBytes ||
+        cudaFuncSetAttribute(s.kernel_m2, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)mk::smem_bytes<SNA>()) != cudaSuccess)
+      return MK_ERR_LAUNCH;
+    // RoPE tables from the allocating path's host_rope (one formula for both
+    // entry points), staged through fixed host buffers and copied with
+    // blocking copies.
+    static float cos_table[kMaxPos * (SNA::D / 2)];
+    static float sin_table[kMaxPos * (SNA::D / 2)];
+    host_rope(SNA::D, 1.0e6, kMaxPos, cos_table, sin_table);
+    if (cudaMemcpy(static_cast<unsigned char*>(p) + kCosOff, cos_table, kRopeBytes, cudaMemcpyHostToDevice) !=
+            cudaSuccess ||
+        cudaMemcpy(static_cast<unsigned char*>(p) + kSinOff, sin_table, kRopeBytes, cudaMemcpyHostToDevice) !=
+            cudaSuccess)
+      return MK_ERR_CUDA;
     s.base = static_cast<unsigned char*>(p);
     s.done = true;
   }
@@ -108,7 +112,10 @@ extern "C" int megakernel_decode_noalloc(const void* d_weights, const long long*
                  "(static scratch) or the KV capacity %d\n", pos + n_steps, kMaxPos, kv_max_seq);
     return MK_ERR_CAPACITY;
   }
-  if ((reinterpret_cast<uintptr_t>(d_weights) & 15) != 0) return MK_ERR_INVALID_ARG;
+  // The kernel's bulk copies read weights and cached K/V at 16-byte
+  // granularity: both buffers must start on a 16-byte boundary.
+  if ((reinterpret_cast<uintptr_t>(d_weights) & 15) != 0 || (reinterpret_cast<uintptr_t>(d_kv) & 15) != 0)
+    return MK_ERR_INVALID_ARG;
   for (int i = 0; i < num_offsets; ++i)
     if (offsets[i] < 0 || (offsets[i] & 15) != 0) return MK_ERR_INVALID_ARG;
   int dev = 0;
@@ -153,7 +160,9 @@ extern "C" int megakernel_decode_noalloc(const void* d_weights, const long long*
   P.trace_steps = 0;
   P.detail = nullptr;
   void* args[] = {&P};
-  if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&mk::decode_kernel<SNA>), dim3(s->sms),
+  const bool m2 = mk::chunks_per_head<SNA>(pos + n_steps - 1) >= mk::kMerge2MinChunks;
+  const void* kern = m2 ? s->kernel_m2 : reinterpret_cast<const void*>(&mk::decode_kernel<SNA>);
+  if (cudaLaunchCooperativeKernel(kern, dim3(s->sms),
                                   dim3(mk::kThreads), args, mk::smem_bytes<SNA>(), st) != cudaSuccess) {
     cudaGetLastError();
     return MK_ERR_LAUNCH;

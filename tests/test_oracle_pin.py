@@ -9,9 +9,9 @@ from oracle.qwen3_decode import Qwen3DecodeOracle, rope_tables
 from ._common import LOGIT_TOL, MARGIN, golden, weights
 
 
-def _teacher_forced(shape_name, n, kv_bf16):
+def _teacher_forced(shape_name, n, kv_bf16, golden_name=None):
     shape, w, _, _ = weights(shape_name)
-    g = golden(shape_name)
+    g = golden(golden_name or shape_name)
     seq = g["seq"].tolist()[:n]
     o = Qwen3DecodeOracle(shape, w, kv_bf16=kv_bf16, max_seq=max(64, n + 1))
     toks, logits, margins = o.run(seq, n)
@@ -24,9 +24,10 @@ def test_tiny_fp32_matches_reference_exactly():
     assert np.array_equal(toks, g["argmax"])
 
 
-@pytest.mark.parametrize("name,n", [("qwen3-0.6b-d64", 12), ("qwen3-0.6b-d128", 6)])
-def test_full_shape_fp32_matches_reference(name, n):
-    g, toks, logits = _teacher_forced(name, n, kv_bf16=False)
+@pytest.mark.parametrize("name,n,gname", [("qwen3-0.6b-d64", 12, None), ("qwen3-0.6b-d128", 6, None),
+                                          ("qwen3-0.6b-d64", 8, "qwen3-0.6b-d64-c1")])
+def test_full_shape_fp32_matches_reference(name, n, gname):
+    g, toks, logits = _teacher_forced(name, n, kv_bf16=False, golden_name=gname)
     err = np.abs(logits[:, g["sub_ids"]] - g["sub_logits"][:n]).max()
     # Same math in fp32 on the same CPU; only summation order differs.
     assert err < 2e-3, err
