@@ -37,12 +37,31 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tok/s, Qwen3-0.6B shape, B=1 on 1×B200; % of HBM roofline"
 PROMPT, GEN = 128, 512
 # Measured DRAM traffic of the decode kernel relative to its algorithmic bytes,
-# from the ncu capture summarised in profiles/decode_kernel_d64_b1.md (one
-# launch of 2 tokens at positions 128-129: 1.958453 GB read + 4.3072 MB
+# from an ncu capture of one launch of 2 tokens at positions 128-129
+# (1.958453 GB read + 4.3072 MB
 # written against 979,346,432 + 979,403,776 algorithmic bytes).  The launch's traffic is
 # scaled from it by the algorithmic bytes of the timed launch (traffic grows
 # with the K/V bytes the same way).
 NCU_TRAFFIC_RATIO = (1_958_453_000 + 4_307_200) / (979_346_432 + 979_403_776)
+
+
+GOLDEN = os.path.join(ROOT, "tests", "golden", "qwen3-0.6b-d64-c1.npz")
+
+
+def parity(tokens):
+    """Greedy tokens of the timed workload (512 after the 128-token prompt)
+    against the reference's fp32 greedy continuation (golden fixture made by
+    host/validate.py's reference_forward path): equal up to the reference's
+    first step whose top-2 margin is <= 1e-2 (the north-star gate)."""
+    g = np.load(GOLDEN)
+    want, margin = g["seq"][PROMPT:PROMPT + GEN], g["margin"][PROMPT - 1:PROMPT + GEN - 1]
+    low = np.nonzero(margin <= 1e-2)[0]
+    upto = int(low[0]) if low.size else GEN
+    got = np.asarray(tokens[:GEN])
+    bad = np.nonzero(got[:upto] != want[:upto])[0]
+    status = "ok" if bad.size == 0 else f"mismatch at generated token {int(bad[0])}"
+    return {"parity": status, "parity_tokens_checked": upto,
+            "parity_tokens_equal_total": int((got == want).sum())}
 
 
 def load_peaks():
@@ -125,44 +144,54 @@ def barrier(world):
         dist.barrier()
 
 
-def cpu_reference(shape, w, prompt, n_new=12, threads=None):
-    """HF bf16 greedy generate on the host cores; returns (tok/s, cores, sample)."""
-    from oracle.hf_reference import build_hf_model, hf_generate
-    threads = threads or os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    model = build_hf_model(shape, w, torch.bfloat16)
-    hf_generate(model, prompt[:8], 2)  # warm up
-    t0 = time.perf_counter()
-    hf_generate(model, prompt, 1)
-    t_prefill = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    hf_generate(model, prompt, n_new + 1)
-    t_all = time.perf_counter() - t0
-    tps = n_new / max(t_all - t_prefill, 1e-9)
-    sample = (f"HF Qwen3ForCausalLM.generate bf16 (host/validate.py:40-52 path), {PROMPT}-token prompt, "
-              f"{n_new} greedy tokens timed (prefill subtracted), torch threads={threads}")
-    return tps, threads, sample
+class CpuReference:
+    """The reference's PyTorch path on the host cores: HF Qwen3ForCausalLM
+    greedy generate in bf16 (host/validate.py:40-52), all host threads."""
+
+    def __init__(self, shape, w, threads=None):
+        from oracle.hf_reference import build_hf_model, hf_generate
+        self.threads = threads or os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.model = build_hf_model(shape, w, torch.bfloat16)
+        self.gen = hf_generate
+        self.gen(self.model, [1, 2, 3, 4], 2)  # warm up
+
+    def run(self, prompt, n_new):
+        """tok/s over n_new greedy tokens after the prompt (prefill time subtracted)."""
+        t0 = time.perf_counter()
+        self.gen(self.model, prompt, 1)
+        t_prefill = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        self.gen(self.model, prompt, n_new + 1)
+        t_all = time.perf_counter() - t0
+        return n_new / max(t_all - t_prefill, 1e-9)
+
+    def sample(self, n_new):
+        return (f"HF Qwen3ForCausalLM.generate bf16 (host/validate.py:40-52 path), {PROMPT}-token prompt, "
+                f"{n_new} greedy tokens timed (positions {PROMPT}..{PROMPT + n_new - 1}, prefill subtracted), "
+                f"torch threads={self.threads}, one CPU stream")
 
 
 def run_reference(args, world, rank):
+    """Rank 0 alone times the reference's CPU path; at N > 1 the value is
+    still one CPU stream (the host cores are shared by all ranks)."""
     if rank != 0:
         return
     from megakernel_b200 import weights as W
     from megakernel_b200.shapes import QWEN3_0_6B_D64 as shape
     w = W.random_weights(shape, 0)
     prompt = W.prompt_ids(shape, PROMPT, seed=1)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        tps, cores, sample = cpu_reference(shape, w, prompt, n_new=args.ref_tokens)
-        if i >= args.warmup:
-            vals.append(tps)
+    ref = CpuReference(shape, w)
+    for _ in range(args.warmup):
+        ref.run(prompt, 8)          # warm-up samples are short
+    vals = [ref.run(prompt, args.ref_tokens) for _ in range(args.steps)]
     v = statistics.median(vals)
     line = {"metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": config_dict(args.gpus),
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
-                             "sample": sample},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.ref_tokens / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": config_dict(args.gpus), "cpu_streams": 1,
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": ref.threads, "kind": "reference",
+                             "sample": ref.sample(args.ref_tokens) + f"; warm-up samples: {args.warmup} x 8 tokens"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -229,11 +258,15 @@ def run_ours(args, world, rank, local):
         e2e_times.append(time.perf_counter() - t0)
     e2e_wall = max_over_ranks(statistics.median(e2e_times), world, dev)
     check = out.cpu().tolist()
-    assert res == [int(first.item())] + check[:GEN - 1], "e2e and device paths disagree"
+    generated = [int(first.item())] + check[:GEN - 1]
+    assert res == generated, "e2e and device paths disagree"
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tps, cores, sample = cpu_reference(shape, w, prompt, n_new=args.ref_tokens)
-        cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference", "sample": sample}
+        ref = CpuReference(shape, w)
+        tps = ref.run(prompt, args.ref_tokens)
+        cpu = {"value": tps, "unit": "tok/s", "cores": ref.threads, "kind": "reference",
+               "sample": ref.sample(args.ref_tokens)}
+        del ref
     traffic = int(NCU_TRAFFIC_RATIO * bytes_launch)
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -250,12 +283,13 @@ def run_ours(args, world, rank, local):
                 "note": "megakernel_generate with host buffers: prompt copy-in, parallel prefill "
                         f"of {PROMPT} tokens (batched tcgen05 steps) + {GEN} greedy tokens, copy-out; wall clock"},
         "gpu_launches": args.steps,
+        **parity(generated),
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
     if world > 1 and not args.no_tp:
         try:
-            line["tensor_parallel"] = run_tp(args, world, rank, local, shape, flat, offs, prompt, check)
+            line["tensor_parallel"] = run_tp(args, world, rank, local, shape, flat, offs, prompt, generated)
         except RuntimeError as e:  # reported, never allowed to drop the headline line
             line["tensor_parallel"] = {"error": str(e)[:200]}
     if rank == 0 and world == 1 and not args.no_batched:
@@ -295,7 +329,7 @@ def run_tp(args, world, rank, local, shape, flat, offs, prompt, single_tokens):
     torch.cuda.synchronize(dev)
     barrier(world)
     ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev), world, dev) / args.steps
-    got = out.cpu().tolist()
+    got = [int(first.item())] + out.cpu().tolist()[:GEN - 1]
     same = sum(1 for a, b in zip(got, single_tokens) if a == b)
     eng.close()
     wb = shape.tp_weight_bytes(world)
@@ -303,7 +337,7 @@ def run_tp(args, world, rank, local, shape, flat, offs, prompt, single_tokens):
                         f"{GEN} greedy tokens (MLP + LM-head rows split, NVLink exchange in-kernel)",
             "value": GEN / (ms / 1e3), "unit": "tok/s", "us_per_token": ms * 1e3 / GEN,
             "weight_bytes_per_gpu": wb, "gpu_launches": args.steps,
-            "greedy_tokens_equal_to_single_gpu": f"{same}/{GEN}"}
+            "greedy_tokens_equal_to_single_gpu": f"{same}/{GEN}", **parity(got)}
 
 
 def run_long(shape, flat, offs, dev, peak):
@@ -377,18 +411,54 @@ def run_batched(shape, flat, offs, dev, peak):
     }
 
 
+def profile_case(args):
+    """Small, bounded launches for profilers (ncu), no timing or JSON line:
+    `b1` decodes --tokens tokens from --pos in one batch-1 launch (~1 GB on
+    the device); `batch` runs --tokens batched steps of --batch sequences at
+    --pos (KV capacity pos + 16)."""
+    from megakernel_b200 import weights as W
+    from megakernel_b200.shapes import QWEN3_0_6B_D64 as shape
+    flat, offs = W.flat_bytes(shape, W.random_weights(shape, 0))
+    dev = torch.device("cuda", 0)
+    if args.profile_case == "b1":
+        from megakernel_b200.bridge import MegakernelEngine
+        eng = MegakernelEngine(flat=flat, offsets=offs, shape=shape, max_seq=args.pos + args.tokens + 8)
+        eng.set_pos(args.pos)
+        out = torch.zeros(args.tokens, dtype=torch.int32, device=dev)
+        eng.decode_n(torch.ones(1, dtype=torch.int32, device=dev), 1, out, n_steps=args.tokens)
+        eng.close()
+    else:
+        from megakernel_b200.batch import BatchDecoder
+        bd = BatchDecoder(flat, offs, batch=args.batch, max_seq=args.pos + args.tokens + 16)
+        bd.set_pos([args.pos] * args.batch)
+        f = torch.randint(0, shape.vocab, (1, args.batch), generator=torch.Generator().manual_seed(1))
+        bd.decode_n(f.to(dev, torch.int32), args.tokens)
+        bd.close()
+    torch.cuda.synchronize()
+    print("profile case ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ref-tokens", type=int, default=12)
+    ap.add_argument("--ref-tokens", type=int, default=GEN,
+                    help="greedy tokens per CPU reference sample (default: the GPU arm's 512)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp", action="store_true", help="skip the configs[4](b) tensor-parallel line (N > 1)")
     ap.add_argument("--no-batched", action="store_true",
                     help="skip the configs[2] long-context and configs[3] batched lines")
+    ap.add_argument("--profile-case", choices=["b1", "batch"], default=None,
+                    help="run one small bounded launch for a profiler and exit")
+    ap.add_argument("--tokens", type=int, default=2)
+    ap.add_argument("--pos", type=int, default=128)
+    ap.add_argument("--batch", type=int, default=64)
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args)
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":

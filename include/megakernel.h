@@ -101,8 +101,8 @@ int megakernel_shape_id(void* handle);
 int megakernel_num_ctas(void* handle);
 
 /* Attention-merge kernel choice for later launches: 0 (default) picks the
- * two-level merge once a launch reaches MK_MERGE2_MIN_CHUNKS (5) split-KV
- * chunks per head (positions > 512) and the direct merge before; 1 always
+ * two-level merge once a launch goes past 5 split-KV chunks per head
+ * (positions > 640) and the direct merge before; 1 always
  * the direct merge; 2 always the kernel instance that carries the two-level
  * merge (it still merges directly below 5 chunks).  Results agree within
  * fp32 rounding; the choice only changes speed.  No reference counterpart. */
@@ -154,7 +154,7 @@ int megakernel_set_trace_detail(void* handle, void* d_buf);
  * d_weights and d_kv must be 16-byte aligned (MK_ERR_INVALID_ARG otherwise);
  * a forced token id outside the vocabulary returns MK_ERR_INVALID_ARG.  Like
  * megakernel_decode_n it runs the kernel instance with the two-level
- * attention merge once pos + n_steps - 1 reaches 5 chunks per head (> 512). */
+ * attention merge once pos + n_steps - 1 goes past 5 chunks per head (> 640). */
 int megakernel_decode_noalloc(const void* d_weights, const long long* offsets, int num_offsets,
                               void* d_kv, int kv_max_seq, int pos, const int* d_tokens,
                               int n_forced, int n_steps, int* d_out, float* d_logits,

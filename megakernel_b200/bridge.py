@@ -149,7 +149,9 @@ class MegakernelEngine:
         """Throughput at several context positions (host/bridge.py:220-261).
 
         Bandwidth counts weights plus K/V bytes (the reference counts a fixed
-        926 MB of weights only, host/bridge.py:229)."""
+        926 MB of weights only, host/bridge.py:229).  Each entry also carries
+        the greedy tokens generated after the all-ones prefix of `position`
+        tokens (an addition, for checking)."""
         if positions is None:
             positions = [1, 10, 50, 100, 500, 1000, 2000]
         res = []
@@ -167,7 +169,8 @@ class MegakernelEngine:
             tps = bench_tokens / elapsed
             nbytes = np.mean([self.shape.algorithmic_bytes(pos + i) for i in range(bench_tokens)])
             res.append({"position": pos, "tok_per_sec": tps, "latency_us": elapsed * 1e6 / bench_tokens,
-                        "bw_gbps": nbytes * tps / 1e9})
+                        "bw_gbps": nbytes * tps / 1e9,
+                        "tokens": outs[pos:pos + bench_tokens].cpu().tolist()})
         return res
 
     def close(self):

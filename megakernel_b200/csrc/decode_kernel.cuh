@@ -1362,7 +1362,16 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
   constexpr int IR = S::I / TP, VR = S::V / TP;
   const int rank = TP > 1 ? P.tp_rank : 0;
   uint32_t kc = 0;
+  // Token ids come from the caller (forced) or from the argmax.  A forced
+  // id outside the vocabulary is never used as an embedding row index: the
+  // launch records MK_ERR_INVALID_ARG (which every CTA's watchdog turns
+  // into an abort) and reads row 0 meanwhile.  (An early-exit path here
+  // measured ~30 us/token slower: this kernel is sensitive to code layout.)
   int tok = P.forced[0];
+  if (tok < 0 || tok >= S::V) {
+    if (tid == 0) atomicCAS(P.err, 0, MK_ERR_INVALID_ARG);
+    tok = 0;
+  }
   #pragma unroll 1
   for (int t = 0; t < P.n_steps; ++t) {
     const int p = P.pos0 + t;
@@ -1371,14 +1380,6 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
     const int nitems = S::NKV * nc;
     const long long clk0 = clock64();
     bool appended = false;
-    // Token ids come from the caller (forced) or from the argmax below; a
-    // forced id outside the vocabulary ends the launch with
-    // MK_ERR_INVALID_ARG before its embedding row is read (every CTA sees
-    // the same id and leaves here).
-    if (tok < 0 || tok >= S::V) {
-      if (tid == 0) fail(P, sm, MK_ERR_INVALID_ARG);
-      return;
-    }
     {
       const __nv_bfloat16* er = sm.wtab[0] + (size_t)tok * S::H;
       for (int i = tid; i < S::H; i += kConsumerThreads) sm.xres[i] = __bfloat162float(er[i]);
@@ -1646,6 +1647,10 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
       const int best = sm.next_token;
       if (cta == 0 && tid == 0) P.out_tokens[t] = best;
       tok = (t + 1 < P.n_forced) ? P.forced[t + 1] : best;
+      if (tok < 0 || tok >= S::V) {
+        if (tid == 0) atomicCAS(P.err, 0, MK_ERR_INVALID_ARG);
+        tok = 0;
+      }
       if (tid == 0) {
         trace_point<S>(P, sm, t, cta, 7 * S::L + 2);
         if (MK_TRACE_POINTS && P.trace != nullptr && t < P.trace_steps) {

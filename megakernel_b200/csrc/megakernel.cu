@@ -352,7 +352,11 @@ int launch(State* st, const int* d_forced, int n_forced, int n_steps, int* d_out
   // The two-level merge kernel once the launch reaches more chunks per head
   // than the threshold at which that merge starts to pay (see shapes.cuh).
   const int nc_last = mk::chunks_per_head<mk::ShapeD64>(st->pos + n_steps - 1);
-  const bool m2 = st->merge_mode == 2 || (st->merge_mode == 0 && nc_last >= mk::kMerge2MinChunks);
+  // Auto: the two-level instance only when the launch goes past
+  // kMerge2MinChunks chunks per head.  Measured on B200 (512-token launch at
+  // positions 128-639, whose last 127 steps have 5 chunks): the two-level
+  // instance took ~30 us/token longer over the launch than the direct one.
+  const bool m2 = st->merge_mode == 2 || (st->merge_mode == 0 && nc_last > mk::kMerge2MinChunks);
   const void* kern = m2 ? st->kernel_m2 : st->kernel;
   cudaError_t e = cudaLaunchCooperativeKernel(kern, dim3(st->ncta), dim3(mk::kThreads), args,
                                               st->smem, stream);

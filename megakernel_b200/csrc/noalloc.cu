@@ -73,7 +73,7 @@ int setup_device(int dev, DeviceSetup** out) {
                              (int)mk::smem_bytes<SNA>()) != cudaSuccess)
       return MK_ERR_LAUNCH;
     // The two-level-merge instance (compiled in tp.cu), used once a call
-    // reaches kMerge2MinChunks chunks per head, as the allocating path does.
+    // goes past kMerge2MinChunks chunks per head, as the allocating path does.
     size_t words = 0;
     s.kernel_m2 = mk_tp::kernel(0, 1, true, &words);
     if (!s.kernel_m2 || words * sizeof(uint64_t) != kHopBytes ||
@@ -160,7 +160,7 @@ extern "C" int megakernel_decode_noalloc(const void* d_weights, const long long*
   P.trace_steps = 0;
   P.detail = nullptr;
   void* args[] = {&P};
-  const bool m2 = mk::chunks_per_head<SNA>(pos + n_steps - 1) >= mk::kMerge2MinChunks;
+  const bool m2 = mk::chunks_per_head<SNA>(pos + n_steps - 1) > mk::kMerge2MinChunks;
   const void* kern = m2 ? s->kernel_m2 : reinterpret_cast<const void*>(&mk::decode_kernel<SNA>);
   if (cudaLaunchCooperativeKernel(kern, dim3(s->sms),
                                   dim3(mk::kThreads), args, mk::smem_bytes<SNA>(), st) != cudaSuccess) {

@@ -77,3 +77,31 @@ def test_batch_decode_n_equals_steps():
     assert np.array_equal(out_n, np.stack(ref, 0))
     assert bd.pos == [7] * 8
     bd.close()
+
+
+def test_batch_long_context_configs3_vs_oracle():
+    """BASELINE configs[3]'s own regime: 64 sequences prefilled to 1,024
+    positions through the batched step (teacher-forced decode_n), then three
+    steps at positions 1024-1026 -- 16 and 17 chunks of 64 positions per
+    (sequence, KV head) through battn_kernel's merge -- compared per
+    sequence with the fp32 oracle run alone on that sequence."""
+    shape, w, flat, offs = weights("qwen3-0.6b-d64")
+    B, P, S = 64, 1024, 3
+    toks = _tokens(B, P + S, seed=11)
+    bd = BatchDecoder(flat, offs, batch=B, max_seq=P + S + 16)
+    bd.decode_n(toks[:, :P].t().contiguous().to(DEV, torch.int32), P)
+    assert bd.pos == [P] * B
+    lgs, outs = [], []
+    for t in range(P, P + S):
+        out, lg = bd.step(toks[:, t].to(DEV), logits=True)
+        lgs.append(lg.cpu().numpy())
+        outs.append(out.cpu().numpy())
+    lg, out = np.stack(lgs, 1), np.stack(outs, 1)
+    bd.close()
+    for b in (0, 37, 63):
+        o = Qwen3DecodeOracle(shape, w, kv_bf16=True, max_seq=P + S + 8, device="cuda")
+        ot, ol, om = o.run(toks[b].tolist(), P + S)
+        err = np.abs(lg[b] - ol[P:]).max()
+        assert err < LOGIT_TOL, (b, err)
+        ok = om[P:] > MARGIN
+        assert np.array_equal(out[b][ok], ot[P:][ok])

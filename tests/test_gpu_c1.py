@@ -5,8 +5,8 @@ Golden vectors: tests/golden/qwen3-0.6b-d64-c1.npz, made by the reference's
 own reference_forward (host/validate.py:33-37) on the fp32 HF model.  At
 these positions every KV head is split into 1..5 chunks of 128 cached
 positions, so both attention merges run: the direct merge (forced for the
-whole launch) and the two-level merge (picked automatically from 5 chunks
-on, or forced from position 0).
+whole launch) and the two-level merge (forced from position 0; picked
+automatically only past 5 chunks, i.e. positions > 640).
 """
 import numpy as np
 import pytest
