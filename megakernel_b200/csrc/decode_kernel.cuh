@@ -120,10 +120,12 @@ struct HopLayout {
   // The GPU-local hops come first, so their offsets do not depend on TP.
   static constexpr long long QKV = 0;                      // [2][QKV]
   static constexpr long long ATT = QKV + 2 * S::QKV;       // [2][items][GRP][D+2]
-  static constexpr long long XA = ATT + 2LL * kAttWords;   // [2][H]  after attention
-  static constexpr long long HM = XA + 2 * S::H;           // [2][I]  silu(g)*u
-  static constexpr long long X = HM + 2 * S::I;            // [2][TP][H]  layer input
-  static constexpr long long LM = X + 2LL * TP * S::H;     // [2][TP * kMaxCtas][2]
+  // The GEMV-input hops that every CTA reads (XA, HM, X) keep one element
+  // per kHopSpread words (shapes.cuh).
+  static constexpr long long XA = ATT + 2LL * kAttWords;   // [2][H]  after attention (spread)
+  static constexpr long long HM = XA + 2LL * S::H * kHopSpread;     // [2][I]  silu(g)*u (spread)
+  static constexpr long long X = HM + 2LL * S::I * kHopSpread;      // [2][TP][H]  layer input (spread)
+  static constexpr long long LM = X + 2LL * TP * S::H * kHopSpread; // [2][TP * kMaxCtas][2]
   static constexpr long long MH = LM + 2LL * TP * kMaxCtas * 2;  // [2][Q]  merged heads (two-level merge)
   static constexpr long long TOTAL = MH + 2LL * S::Q;
 };
@@ -194,6 +196,17 @@ struct Smem {
   volatile int done;                  // consumers finished (watchdog exits)
   unsigned long long wait_hop_ns;     // trace accounting (thread 0)
   const __nv_bfloat16* wtab[S::NOFF]; // weight pointer table (offsets order)
+  // The copy engine's schedule, computed once per launch (every division by
+  // the CTA count happens here, none in the producer's loops): rows [r0, r1)
+  // of GEMV phase ph (0 q/k/v, 1 O, 2 gate/up, 3 down) at layer l packed as
+  // r0 | r1 << 16 in rows[4 l + ph], the rotated CTA index that places
+  // attention items per layer, the LM-head rows, and division magics
+  // (magic_of) for the CTA count and for 1..16 chunks per head.
+  uint32_t rows[4 * S::L];
+  uint16_t itc[S::L];
+  int lm0, lm1;
+  uint32_t magic_n;
+  uint32_t magic_c[kMaxChunksPerHead + 1];
   KParams prm;                        // copy of the launch parameters
   alignas(8) unsigned char prod[64];  // the producer's state (see Producer)
   alignas(8) uint64_t full[S::NST];
@@ -283,156 +296,156 @@ __device__ __forceinline__ size_t kv_index(int l, int kind, int h, int pos, int 
 
 namespace mk {
 
+// ---- schedule helpers ---------------------------------------------------------
+// floor(x / d) for the small numerators of the schedule, from
+// m = ceil(2^31 / d): floor(2x m / 2^32), exact while x d < 2^31 (x < 2^31).
+__host__ __device__ __forceinline__ uint32_t magic_of(uint32_t d) {
+  return (uint32_t)((0x80000000ull + d - 1) / d);
+}
+__device__ __forceinline__ uint32_t divm(uint32_t x, uint32_t m) { return __umulhi(x << 1, m); }
+
 // ---- producer ---------------------------------------------------------------
-// The copy issuer, one thread.  Its methods stay out of line so the kernel's
-// code (shared instruction caches with the consumer warps) stays small.
-template <class S>
-struct Producer {
-  const KParams* P;
-  Smem<S>* sm;
-  uint8_t* ring;
-  uint64_t pol;
-  uint32_t nst;
-  uint32_t k;       // stages issued so far
-  bool ok;
-  uint64_t last;    // globaltimer of the last issue (pacing)
-
-  __device__ __forceinline__ bool acquire(uint32_t& slot) {
-    slot = k % nst;
-    const uint32_t ph = (k / nst) & 1u;
-    if (!wait_bar(*P, *sm, &sm->empty[slot], ph ^ 1u)) ok = false;
-    // Pacing: spread ring refills out instead of re-issuing every freed stage
-    // at once, so weight reads do not flood the memory system in bursts
-    // exactly when activations are being exchanged.
-    if (ok && P->issue_gap_ns > 0) {
-      uint64_t now = globaltimer_ns();
-      while (now - last < (uint64_t)P->issue_gap_ns) now = globaltimer_ns();
-      last = now;
-    }
-    return ok;
-  }
-  // Contiguous bytes (LM-head rows, cached K/V): one copy per stage.
-  __device__ __forceinline__ void issue(const void* src, uint32_t bytes) {
-    uint32_t slot;
-    if (!ok || !acquire(slot)) return;
-    mbar_arrive_expect_tx(&sm->full[slot], bytes);
-    bulk_g2s(ring + (size_t)slot * S::STB, src, bytes, &sm->full[slot], pol);
-    ++k;
-  }
-  __device__ __forceinline__ void rows(const __nv_bfloat16* base, int r0, int r1, int K) {
-    const int rpc = S::STB / (2 * K);
-    for (int r = r0; r < r1 && ok; r += rpc) {
-      const int n = min(rpc, r1 - r);
-      issue(base + (size_t)r * K, (uint32_t)(n * 2 * K));
-    }
-  }
-  // Rows for the tensor-core GEMV: one copy per row, at pitch 2K + 16.  Row
-  // r starts at base + r * stride (stride > K: a column slice of each row).
-  __device__ __forceinline__ void rows_padded(const __nv_bfloat16* base, int r0, int r1, int K,
-                                              int stride = 0) {
-    if (stride == 0) stride = K;
-    const int pitch = 2 * K + kRowPad;
-    const int rpc = S::STB / pitch;
-    for (int r = r0; r < r1 && ok; r += rpc) {
-      const int n = min(rpc, r1 - r);
-      uint32_t slot;
-      if (!acquire(slot)) return;
-      mbar_arrive_expect_tx(&sm->full[slot], (uint32_t)(n * 2 * K));
-      for (int i = 0; i < n; ++i)
-        bulk_g2s(ring + (size_t)slot * S::STB + (size_t)i * pitch, base + (size_t)(r + i) * stride,
-                 (uint32_t)(2 * K), &sm->full[slot], pol);
-      ++k;
-    }
-  }
-  // Cached K/V of attention items [ilo, ihi) of layer l at step t.  Positions
-  // < p-1 were written by steps <= t-2 of this launch (or earlier launches):
-  // wait until the consumers have finished step t-2 before reading them.
-  // Position p-1 is read by the consumers directly (written by step t-1).
-  __device__ __forceinline__ void kv_items(int t, int l, int p, int nc, int ilo, int ihi) {
-    for (int i = ilo; i < ihi && ok; ++i) {
-      const int h = i / nc, j = i % nc;
-      int c0, c1;
-      chunk_range(p, nc, j, c0, c1);
-      const int te = min(c1, p - 1);
-      if (c0 >= te) continue;
-      if (t >= 2) {
-        Spin sp;
-        while (sm->tokens_done < t - 1) {
-          if (!sp.keep_going(*P, *sm)) { ok = false; return; }
-        }
-        fence_proxy_async_global();
-      }
-      for (int a = c0; a < te && ok; a += S::SUBP) {
-        const int n = min(S::SUBP, te - a);
-        issue(P->kv + kv_index<S>(l, 0, h, a, P->max_seq), (uint32_t)(n * S::D * 2));
-        issue(P->kv + kv_index<S>(l, 1, h, a, P->max_seq), (uint32_t)(n * S::D * 2));
-      }
-    }
-  }
-  // Abandoned: wait (bounded) for the copies already in flight so that no
-  // bulk copy lands in shared memory after this CTA has exited.
-  __device__ __forceinline__ void drain() {
-    const uint32_t first = k > nst ? k - nst : 0;
-    for (uint32_t c = first; c < k; ++c) {
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(&sm->full[c % nst], (c / nst) & 1u)) {
-        if ((long long)(globaltimer_ns() - t0) > P->timeout_ns) break;
-      }
-    }
-  }
-};
-
+// The copy issuer, one thread.  It walks this CTA's byte stream in the order
+// the consumers use it -- per layer the q, k, v rows, the cached K/V of its
+// attention items, the O rows, the gate and up rows and the down rows; per
+// step the LM-head rows -- as a sequence of "segments", each a run of ring
+// stages described by a few numbers, and issues every stage from one place:
+// the producer's code is small because it shares the SM's instruction cache
+// with the consumer warps (an earlier form, one inlined copy loop per weight
+// matrix, was 39 KB of the kernel).  Stage q of a segment copies
+//   cnt = min(per, total - g per) units,  g = q >> kv,
+//   from base + (q & kv) kind_stride + g per unit_stride,
+// either as cnt pieces of piece_bytes at row_stride, placed at `pitch` in the
+// stage (weight rows for the tensor-core GEMV), or as one copy of
+// cnt * unit_bytes bytes (LM-head rows, cached K/V).  kv = 1 interleaves the
+// K and V streams of an attention item.  Bulk copies only, never multicast.
+// With TP > 1 this GPU reads its rank's slice of the MLP (rows of gate/up,
+// columns of down) and of the LM head.
 template <class S, int TP>
 __device__ __forceinline__ void producer(const KParams& P, Smem<S>& sm, uint8_t* ring, int cta) {
-  // With TP > 1 this GPU reads its rank's slice of the MLP (rows of gate/up,
-  // columns of down) and of the LM head (vocab rows); the rest is replicated.
   constexpr int IR = S::I / TP, VR = S::V / TP;
+  constexpr int LPC = S::STB / (2 * S::H);
+  constexpr int RPC_H = S::STB / (2 * S::H + kRowPad), RPC_Q = S::STB / (2 * S::Q + kRowPad),
+                RPC_I = S::STB / (2 * IR + kRowPad);
   const int rank = TP > 1 ? P.tp_rank : 0;
   if ((threadIdx.x & 31) != 0) return;
-  const int N = P.ncta;
-  // Its state lives in shared memory: the methods take `this`, and a stack
-  // object would be local memory, which misses the nearly absent L1.
-  static_assert(sizeof(Producer<S>) <= sizeof(sm.prod), "producer state");
-  Producer<S>& pr = *reinterpret_cast<Producer<S>*>(sm.prod);
-  pr.k = 0;
-  pr.ok = true;
-  pr.last = 0;
-  pr.P = &P;
-  pr.sm = &sm;
-  pr.ring = ring;
-  pr.pol = policy_evict_first();
-  pr.nst = (uint32_t)P.nst;
+  const uint64_t pol = policy_evict_first();
+  const uint32_t nst = (uint32_t)P.nst;
+  uint32_t slot = 0, par = 0, issued = 0;
+  bool ok = true;
+  Spin spin;
 #pragma unroll 1
-  for (int t = 0; t < P.n_steps && pr.ok; ++t) {
+  for (int t = 0; t < P.n_steps && ok; ++t) {
     const int p = P.pos0 + t;
     const int nc = chunks_per_head<S>(p);
-    const int nitems = S::NKV * nc;
+    const uint32_t mc = sm.magic_c[nc];
+    // seg 0-2 q, k, v; 3 the attention items' K/V (item index in `it`);
+    // 4 O; 5 gate; 6 up; 7 down; then (l == L) the LM head.
+    int l = 0, seg = 0, it = 0, ihi = 0;
+    trace_point<S>(P, sm, t, cta, 0);
 #pragma unroll 1
-    for (int l = 0; l < S::L && pr.ok; ++l) {
-      trace_point<S>(P, sm, t, cta, 7 * l);
-      int r0, r1;
-      split_rows(S::QKV, N, cta, phase_rot(l, 0, N), r0, r1);
-#pragma unroll 1
-      for (int m = 0; m < 3; ++m) {
-        int a, b, o;
-        if (qkv_part<S>(r0, r1, m, a, b, o)) pr.rows_padded(wptr(l, W_Q + m), a, b, S::H);
+    while (ok) {
+      const char* base = nullptr;
+      size_t kind_stride = 0, unit_stride = 0, row_stride = 0;
+      int total = 0, per = 1, kv = 0, pitch = 0;
+      uint32_t unit_bytes = 0, piece_bytes = 0;
+      bool pieces = false;
+      if (l == S::L) {                                   // LM-head rows
+        base = reinterpret_cast<const char*>(sm.wtab[0] + (size_t)(rank * VR + sm.lm0) * S::H);
+        total = sm.lm1 - sm.lm0;
+        per = LPC;
+        unit_bytes = 2 * S::H;
+        unit_stride = 2 * S::H;
+      } else if (seg == 3) {                             // cached K/V of item `it`
+        if (it == 0 && ihi == 0) {
+          const uint32_t c = sm.itc[l], nit = (uint32_t)(S::NKV * nc);
+          it = (int)divm(c * nit + P.ncta - 1, sm.magic_n);
+          ihi = (int)divm((c + 1) * nit + P.ncta - 1, sm.magic_n);
+        }
+        if (it < ihi) {
+          const int h = (int)divm(it, mc), j = it - h * nc;
+          const int c0 = (int)divm(j * p, mc);
+          const int te = min((int)divm((j + 1) * p, mc), p - 1);
+          total = te - c0;
+          if (total > 0 && t >= 2) {
+            // Positions < p-1 were written by steps <= t-2 (or earlier
+            // launches): wait until the consumers have finished step t-2.
+            // Position p-1 is read by the consumers directly.
+            while (sm.tokens_done < t - 1)
+              if (!spin.keep_going(P, sm)) { ok = false; break; }
+            fence_proxy_async_global();
+          }
+          base = reinterpret_cast<const char*>(P.kv + kv_index<S>(l, 0, h, c0, P.max_seq));
+          kind_stride = (size_t)S::NKV * P.max_seq * S::D * 2;
+          per = S::SUBP;
+          unit_bytes = S::D * 2;
+          unit_stride = S::D * 2;
+          kv = 1;
+        }
+      } else {                                           // weight rows
+        const int ph = seg < 3 ? 0 : seg - 3 - (seg >= 6 ? 1 : 0);
+        const uint32_t rr = sm.rows[4 * l + ph];
+        int r0 = (int)(rr & 0xffffu), r1 = (int)(rr >> 16);
+        int K = S::H, wkey = W_Q + seg;
+        row_stride = S::H;
+        if (seg < 3) {
+          int a, b, o;
+          if (qkv_part<S>(r0, r1, seg, a, b, o)) { r0 = a; r1 = b; } else { r1 = r0; }
+        } else if (seg == 4) {
+          K = S::Q; row_stride = S::Q; wkey = W_O;
+        } else if (seg < 7) {
+          wkey = seg == 5 ? W_GATE : W_UP;
+          r0 += rank * IR; r1 += rank * IR;
+        } else {
+          K = IR; row_stride = S::I; wkey = W_DOWN;
+        }
+        const __nv_bfloat16* wb = wptr(l, wkey) + (seg == 7 ? (size_t)rank * IR : 0);
+        base = reinterpret_cast<const char*>(wb + (size_t)r0 * row_stride);
+        total = r1 - r0;
+        per = seg == 4 ? RPC_Q : (seg == 7 ? RPC_I : RPC_H);
+        piece_bytes = 2 * K;
+        row_stride *= 2;
+        unit_stride = row_stride;
+        pitch = 2 * K + kRowPad;
+        pieces = true;
       }
-      int ilo, ihi;
-      items_of_cta(cta, l, nitems, N, ilo, ihi);
-      pr.kv_items(t, l, p, nc, ilo, ihi);
-      split_rows(S::H, N, cta, phase_rot(l, 1, N), r0, r1);
-      pr.rows_padded(wptr(l, W_O), r0, r1, S::Q);
-      split_rows(IR, N, cta, phase_rot(l, 2, N), r0, r1);
-      pr.rows_padded(wptr(l, W_GATE), rank * IR + r0, rank * IR + r1, S::H);
-      pr.rows_padded(wptr(l, W_UP), rank * IR + r0, rank * IR + r1, S::H);
-      split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
-      pr.rows_padded(wptr(l, W_DOWN) + (size_t)rank * IR, r0, r1, IR, S::I);
+      // ---- the segment's stages, issued from this one place ----
+#pragma unroll 1
+      for (int q = 0; ok && total > 0; ++q) {
+        const int g = q >> kv;
+        const int cnt = min(per, total - g * per);
+        if (cnt <= 0) break;
+        if (!wait_bar(P, sm, &sm.empty[slot], par ^ 1u)) { ok = false; break; }
+        const char* src = base + (size_t)(q & kv) * kind_stride + (size_t)g * per * unit_stride;
+        uint8_t* dst = ring + (size_t)slot * S::STB;
+        const int n = pieces ? cnt : 1;
+        const uint32_t bytes = pieces ? piece_bytes : (uint32_t)cnt * unit_bytes;
+        mbar_arrive_expect_tx(&sm.full[slot], (uint32_t)n * bytes);
+        for (int i = 0; i < n; ++i)
+          bulk_g2s(dst + (size_t)i * pitch, src + (size_t)i * row_stride, bytes, &sm.full[slot], pol);
+        ++issued;
+        if (++slot == nst) { slot = 0; par ^= 1u; }
+      }
+      // ---- next segment ----
+      if (l == S::L) break;
+      if (seg == 3 && it < ihi) { ++it; if (it < ihi) continue; }
+      if (++seg == 8) {
+        seg = 0; it = 0; ihi = 0;
+        ++l;
+        if (l < S::L) trace_point<S>(P, sm, t, cta, 7 * l);
+      }
     }
-    int r0, r1;
-    split_rows(VR, N, cta, phase_rot(S::L, 4, N), r0, r1);
-    pr.rows(sm.wtab[0], rank * VR + r0, rank * VR + r1, S::H);
   }
-  if (!pr.ok) pr.drain();
+  if (!ok) {
+    // Abandoned: wait (bounded) for the copies already in flight so that no
+    // bulk copy lands in shared memory after this CTA has exited.
+    const uint32_t first = issued > nst ? issued - nst : 0;
+    for (uint32_t c = first; c < issued; ++c) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&sm.full[c % nst], (c / nst) & 1u))
+        if ((long long)(globaltimer_ns() - t0) > P.timeout_ns) break;
+    }
+  }
 }
 
 }  // namespace mk
@@ -486,13 +499,13 @@ __device__ MK_PHASE void wait_tagged(const KParams& P, Smem<S>& sm, const uint64
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
       const int i = base + k * kConsumerThreads;
-      v[k] = i < n ? ld_relaxed(src + i) : 0;
+      v[k] = i < n ? ld_relaxed(src + (size_t)i * kHopSpread) : 0;
     }
     const uint64_t* sp[kBatch];
     int nv = 0;
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
-      sp[k] = src + base + k * kConsumerThreads;
+      sp[k] = src + (size_t)(base + k * kConsumerThreads) * kHopSpread;
       nv += (base + k * kConsumerThreads < n) ? 1 : 0;
     }
     resolve_tagged<S, kBatch>(P, sm, v, sp, nv, tag);
@@ -779,13 +792,13 @@ __device__ __forceinline__ float hop_to_xs(const KParams& P, Smem<S>& sm, const 
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
       const int i = base + k * kConsumerThreads;
-      w[k] = i < n ? ld_relaxed(src + i) : 0;
+      w[k] = i < n ? ld_relaxed(src + (size_t)i * kHopSpread) : 0;
     }
     const uint64_t* sp[kBatch];
     int nv = 0;
 #pragma unroll
     for (int k = 0; k < kBatch; ++k) {
-      sp[k] = src + base + k * kConsumerThreads;
+      sp[k] = src + (size_t)(base + k * kConsumerThreads) * kHopSpread;
       nv += (base + k * kConsumerThreads < n) ? 1 : 0;
     }
     resolve_tagged<S, kBatch>(P, sm, w, sp, nv, tag);
@@ -827,7 +840,7 @@ __device__ __forceinline__ float hop_sum_to_xs(const KParams& P, Smem<S>& sm, co
     for (int e = 0; e < EG; ++e)
 #pragma unroll
       for (int j = 0; j < TP; ++j) {
-        sp[e * TP + j] = src + (size_t)j * S::H + threadIdx.x + (e0 + e) * kConsumerThreads;
+        sp[e * TP + j] = src + ((size_t)j * S::H + threadIdx.x + (e0 + e) * kConsumerThreads) * kHopSpread;
         w[e * TP + j] = ld_relaxed_sys(sp[e * TP + j]);
       }
     resolve_tagged<S, EG * TP, true>(P, sm, w, sp, EG * TP, tag);
@@ -1407,10 +1420,10 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         float ss = 0.f;
         if (l > 0) {
           if constexpr (TP == 1)
-            ss = hop_to_xs<S, true, true, GainRegs<S>::kPer>(P, sm, P.hop + HopLayout<S>::X + (size_t)(l & 1) * S::H, S::H,
+            ss = hop_to_xs<S, true, true, GainRegs<S>::kPer>(P, sm, P.hop + HopLayout<S>::X + (size_t)(l & 1) * S::H * kHopSpread, S::H,
                                           tag_of(seq, l - 1, 4), gains);
           else
-            ss = hop_sum_to_xs<S, TP, true>(P, sm, P.hop + HopLayout<S, TP>::X + (size_t)(l & 1) * TP * S::H,
+            ss = hop_sum_to_xs<S, TP, true>(P, sm, P.hop + HopLayout<S, TP>::X + (size_t)(l & 1) * TP * S::H * kHopSpread,
                                             tag_of(seq, l - 1, 4), gains);
         } else {
 #pragma unroll
@@ -1463,10 +1476,10 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 3);
         kc += gp.finish(P, sm, sm.rowsum[0], nullptr, nullptr, false);
         MK_DP(10);
-        uint64_t* dst = P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H;
+        uint64_t* dst = P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H * kHopSpread;
         const uint32_t tg = tag_of(seq, l, 2);
         for (int r = tid; r < r1 - r0; r += kConsumerThreads)
-          st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
+          st_tagged(dst + (size_t)(r0 + r) * kHopSpread, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
         if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 4);
       }
       // ---- P4: x' -> RMSNorm -> silu(gate) * up ---------------------------------
@@ -1479,20 +1492,20 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         // xres is rewritten by the hop below: every thread must be done with
         // the O epilogue's reads of it.
         consumer_sync(kConsumerThreads);
-        const float ss = hop_to_xs<S, true, true, GainRegs<S>::kPer>(P, sm, P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H,
+        const float ss = hop_to_xs<S, true, true, GainRegs<S>::kPer>(P, sm, P.hop + HopLayout<S>::XA + (size_t)(l & 1) * S::H * kHopSpread,
                                                   S::H, tag_of(seq, l, 2), gains);
         norm_partial(sm, ss);
         if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
         MK_DP(13);
         kc += gp.finish(P, sm, sm.rowsum[0], sm.rowsum[1], nullptr, true);
         MK_DP(15);
-        uint64_t* dst = P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I;
+        uint64_t* dst = P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I * kHopSpread;
         const uint32_t tg = tag_of(seq, l, 3);
         for (int r = tid; r < r1 - r0; r += kConsumerThreads) {
           const float g = sm.rowsum[0][r];
           const float u = sm.rowsum[1][r];
           const float hval = (g / (1.0f + expf(-g))) * u;
-          st_tagged(dst + r0 + r, tg, __float_as_uint(hval));
+          st_tagged(dst + (size_t)(r0 + r) * kHopSpread, tg, __float_as_uint(hval));
         }
         if (tid == 0) trace_point<S>(P, sm, t, cta, 7 * l + 5);
       }
@@ -1502,29 +1515,29 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
         split_rows(S::H, N, cta, phase_rot(l, 3, N), r0, r1);
         GemvPlan<S, IR, 2> gp;
         gp.prepare(P, sm, ring, kc, r1 - r0, 0, 0);
-        hop_to_xs<S, false, false, (IR + kConsumerThreads - 1) / kConsumerThreads>(P, sm, P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I, IR,
+        hop_to_xs<S, false, false, (IR + kConsumerThreads - 1) / kConsumerThreads>(P, sm, P.hop + HopLayout<S>::HM + (size_t)(l & 1) * S::I * kHopSpread, IR,
                                    tag_of(seq, l, 3), gains);
         if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
         MK_DP(17);
         kc += gp.finish(P, sm, sm.rowsum[0], nullptr, nullptr, false);
         MK_DP(18);
-        uint64_t* dst = P.hop + HopLayout<S>::X + (size_t)((l + 1) & 1) * S::H;
+        uint64_t* dst = P.hop + HopLayout<S>::X + (size_t)((l + 1) & 1) * S::H * kHopSpread;
         const uint32_t tg = tag_of(seq, l, 4);
         const bool skip = (l == 0 && cta == P.debug_skip_cta);
         if constexpr (TP == 1) {
           if (!skip)
             for (int r = tid; r < r1 - r0; r += kConsumerThreads)
-              st_tagged(dst + r0 + r, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
+              st_tagged(dst + (size_t)(r0 + r) * kHopSpread, tg, __float_as_uint(sm.xres[r0 + r] + sm.rowsum[0][r]));
         } else {
           // This rank's partial rows (no residual: every rank adds x' itself)
           // into slot `rank` of every GPU's X hop, over NVLink for the peers.
           (void)dst;
-          const size_t off = HopLayout<S, TP>::X + (size_t)((l + 1) & 1) * TP * S::H + (size_t)rank * S::H + r0;
+          const size_t off = HopLayout<S, TP>::X + ((size_t)((l + 1) & 1) * TP * S::H + (size_t)rank * S::H + r0) * kHopSpread;
           if (!skip)
             for (int r = tid; r < r1 - r0; r += kConsumerThreads)
 #pragma unroll
               for (int j = 0; j < TP; ++j)
-                st_tagged_sys(P.peer_hop[j] + off + r, tg, __float_as_uint(sm.rowsum[0][r]));
+                st_tagged_sys(P.peer_hop[j] + off + (size_t)r * kHopSpread, tg, __float_as_uint(sm.rowsum[0][r]));
         }
         // xres is rewritten by the next layer's hop: finish the reads first.
         consumer_sync(kConsumerThreads);
@@ -1543,10 +1556,10 @@ __device__ __forceinline__ void consumers(const KParams& P, Smem<S>& sm, const u
     GainRegs<S> fgains;
     fgains.load(sm.wtab[1]);
     if constexpr (TP == 1)
-      wait_tagged(P, sm, P.hop + HopLayout<S>::X + (size_t)(S::L & 1) * S::H, S::H,
+      wait_tagged(P, sm, P.hop + HopLayout<S>::X + (size_t)(S::L & 1) * S::H * kHopSpread, S::H,
                   tag_of(seq, S::L - 1, 4), sm.xres);
     else
-      hop_sum_to_xs<S, TP, false>(P, sm, P.hop + HopLayout<S, TP>::X + (size_t)(S::L & 1) * TP * S::H,
+      hop_sum_to_xs<S, TP, false>(P, sm, P.hop + HopLayout<S, TP>::X + (size_t)(S::L & 1) * TP * S::H * kHopSpread,
                                   tag_of(seq, S::L - 1, 4), fgains);
     if (consumer_any(kConsumerThreads, sm.abort_flag != 0)) return;
     rmsnorm_to_xin(sm, fgains);
@@ -1706,6 +1719,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   Smem<S>& sm = *reinterpret_cast<Smem<S>*>(dsm + (size_t)S::NST * S::STB);
   for (int i = threadIdx.x; i < S::NOFF; i += blockDim.x) sm.wtab[i] = P.w[i];
   if (threadIdx.x == 0) sm.prm = P;
+  {
+    // The producer's schedule (see Smem::rows): the same split_rows /
+    // phase_rot / items_of_cta plan the consumers follow.
+    constexpr int IR = S::I / TP, VR = S::V / TP;
+    const int N = P.ncta, i = threadIdx.x;
+    if (i < 4 * S::L) {
+      const int l = i >> 2, ph = i & 3;
+      const int R = ph == 0 ? S::QKV : (ph == 2 ? IR : S::H);
+      int r0, r1;
+      split_rows(R, N, blockIdx.x, phase_rot(l, ph, N), r0, r1);
+      sm.rows[i] = (uint32_t)r0 | ((uint32_t)r1 << 16);
+    } else if (i < 5 * S::L) {
+      const int l = i - 4 * S::L;
+      sm.itc[l] = (uint16_t)(((unsigned)blockIdx.x + (unsigned)N - (unsigned)(l * 53) % (unsigned)N) % (unsigned)N);
+    } else if (i == 5 * S::L) {
+      split_rows(VR, N, blockIdx.x, phase_rot(S::L, 4, N), sm.lm0, sm.lm1);
+      sm.magic_n = magic_of((uint32_t)N);
+    } else if (i > 5 * S::L && i <= 5 * S::L + kMaxChunksPerHead) {
+      const uint32_t d = (uint32_t)(i - 5 * S::L);
+      sm.magic_c[d] = magic_of(d);
+    }
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::NST; ++s) {
       mbar_init(&sm.full[s], 1);

@@ -24,6 +24,14 @@ constexpr int kRingBytes = 176 * 1024;
 constexpr int kMaxCtas = 256;
 constexpr int kRowsMax = 256;           // weight rows one CTA owns in one phase
 constexpr int kRowPad = 16;             // bytes between weight rows in a ring stage
+// 64-bit words between consecutive elements of the all-read activation hops.
+// A microbenchmark of a bare 148-CTA all-gather ran faster with elements one
+// per 32-byte sector (4), but in this kernel 4 measured 530 against 510
+// us/token for 1 (B200, 512-token launch at positions 128-639).
+#ifndef MK_HOP_SPREAD
+#define MK_HOP_SPREAD 1
+#endif
+constexpr int kHopSpread = MK_HOP_SPREAD;
 constexpr int kMaxTP = 8;               // tensor-parallel GPUs at most
 constexpr int kPvParts = 4;             // position parts of the attention P.V (warps / GRP)
 constexpr int kMaxChunksPerHead = 16;   // attention split-KV chunks per KV head
