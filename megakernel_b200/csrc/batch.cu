@@ -274,25 +274,33 @@ struct EpiArgmax {
 };
 
 // Split-KV attention on tensor cores, one warp per item (sequence b, KV head
-// h, chunk c of 64 positions <= pos_b) for the GQA pair of query heads
-// (2h, 2h+1).  Replaces warp_attention (src/attention.cuh:100-167) for many
-// sequences at once.
-//   - K and V of the chunk go to this warp's shared memory with cp.async
-//     (64 rows of 128 B each, 16-byte chunks XOR-swizzled by row so ldmatrix
-//     is bank-conflict free); rows past pos are copied too but masked;
+// h, span s of `span` chunks of 64 positions <= pos_b) for the GQA pair of
+// query heads (2h, 2h+1).  Replaces warp_attention (src/attention.cuh:100-167)
+// for many sequences at once.
+//   - the warp walks its span's chunks with an online softmax, K and V of the
+//     next chunk arriving by cp.async into the other half of a double buffer
+//     while the current chunk is computed (64 rows of 128 B each, 16-byte
+//     chunks XOR-swizzled by row so ldmatrix is bank-conflict free); rows
+//     past pos are copied too but masked;
 //   - S = Q K^T and O = P V run as mma.sync m16n8k16 (bf16, fp32 accumulate).
 //     Q and P enter as two bf16 rows each (hi = bf16(v), lo = bf16(v - hi);
 //     rows 0/1 = hi of heads 0/1, rows 2/3 = lo) so the products keep ~16
 //     mantissa bits; the score accumulators are reused as the A operand of
 //     P V (same fragment layout);
-//   - the partial {acc[2][64], m[2], l[2]} goes to part[b][h][c]; the warp
-//     that completes the last chunk of (b, h) (ticket in acnt) merges all
-//     chunks in chunk order and writes hi/lo of the two heads' outputs into
-//     a_att -- no separate merge pass.
-constexpr int kBAttnWarps = 4;
+//   - a span that covers the whole context writes hi/lo of the two heads'
+//     outputs into a_att directly; otherwise the partial {acc[2][64], m[2],
+//     l[2]} goes to part[b][h][s] and the warp that completes the last span
+//     of (b, h) (ticket in acnt) merges all spans in span order -- no
+//     separate merge pass.
+constexpr int kBAttnWarps = 2;
+#ifndef MK_BATTN_BUFS
+#define MK_BATTN_BUFS 3
+#endif
+constexpr int kBAttnBufs = MK_BATTN_BUFS;   // chunks of K/V per warp: current + in flight
+constexpr int kBAttnBlocksPerSm = kBAttnBufs == 2 ? 3 : 2;
 struct AttnWarpSmem {
-  alignas(128) __nv_bfloat16 k[kBChunk * kBD];  // 8 KB, swizzled
-  alignas(128) __nv_bfloat16 v[kBChunk * kBD];  // 8 KB, swizzled
+  alignas(128) __nv_bfloat16 k[kBAttnBufs][kBChunk * kBD];  // 8 KB each, swizzled
+  alignas(128) __nv_bfloat16 v[kBAttnBufs][kBChunk * kBD];
   alignas(16) float q[2][kBD];
 };
 constexpr size_t kBAttnSmem = sizeof(AttnWarpSmem) * kBAttnWarps;
@@ -305,9 +313,9 @@ __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_n() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 // byte offset of (row, 16-byte chunk) in a swizzled 64 x 128 B tile
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -331,8 +339,7 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
 // chunks' (m, l) in parallel (32 chunks per round), then every lane sums its
 // two output dimensions over the chunks with the weights broadcast by
 // shuffle, loads batched eight chunks at a time.  Fixed summation order.
-__device__ __forceinline__ void attn_merge(const BatchDev& d, int b, int h, int lane) {
-  const int nc = d.pos[b] / kBChunk + 1;
+__device__ __forceinline__ void attn_merge(const BatchDev& d, int b, int h, int lane, int nc) {
   const float* base = d.part + ((size_t)b * kBNKV + h) * d.maxch * 132;
   float M[2] = {-INFINITY, -INFINITY};
   for (int c0 = 0; c0 < nc; c0 += 32) {
@@ -387,34 +394,45 @@ __device__ __forceinline__ void attn_merge(const BatchDev& d, int b, int h, int 
   }
 }
 
-__global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int l) {
+__global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int l, int span) {
   extern __shared__ __align__(128) uint8_t attn_smem_raw[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int g = lane >> 2, tq = lane & 3;
   AttnWarpSmem& sw = reinterpret_cast<AttnWarpSmem*>(attn_smem_raw)[wid];
-  const uint32_t ks = smem_u32(sw.k), vs = smem_u32(sw.v);
   const int wglob = blockIdx.x * kBAttnWarps + wid;
   const int nw = gridDim.x * kBAttnWarps;
-  const int nitems = kBMax * kBNKV * d.maxch;
+  const int maxspan = (d.maxch + span - 1) / span;
+  const int nitems = kBMax * kBNKV * maxspan;
   pdl_launch();
   pdl_wait();
   for (int it = wglob; it < nitems; it += nw) {
-    const int c = it % d.maxch, h = (it / d.maxch) % kBNKV, b = it / (d.maxch * kBNKV);
+    const int s = it % maxspan, h = (it / maxspan) % kBNKV, b = it / (maxspan * kBNKV);
     if (b >= d.batch) continue;
     const int p = d.pos[b];
-    const int c0 = c * kBChunk;
-    if (c0 > p) continue;
-    const int n = min(kBChunk, p + 1 - c0);
+    const int nc = p / kBChunk + 1;              // chunks holding positions 0..p
+    const int cs = s * span;
+    if (cs >= nc) continue;
+    const int ce = min(nc, cs + span);
+    const int nspan = (nc + span - 1) / span;
     const __nv_bfloat16* Kc = d.kv + bkv_index(d, b, l, 0, h, 0);
     const __nv_bfloat16* Vc = d.kv + bkv_index(d, b, l, 1, h, 0);
     __syncwarp();   // the previous item's readers of sw are done
-    // 64 rows x 8 chunks of K and of V; rows past max_seq clamp (masked later)
+    // K and V of chunk c (64 rows x 8 chunks of 16 B each) into buffer `buf`;
+    // rows past max_seq clamp (masked later).
+    auto load = [&](int c, int buf) {
+      const uint32_t ks = smem_u32(sw.k[buf]), vs = smem_u32(sw.v[buf]);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int idx = lane + 32 * k, row = idx >> 3, ch = idx & 7;
-      const int src_row = min(c0 + row, d.max_seq - 1);
-      cp_async16(ks + swz(row, ch), Kc + (size_t)src_row * kBD + ch * 8);
-      cp_async16(vs + swz(row, ch), Vc + (size_t)src_row * kBD + ch * 8);
+      for (int k = 0; k < 16; ++k) {
+        const int idx = lane + 32 * k, row = idx >> 3, ch = idx & 7;
+        const int src_row = min(c * kBChunk + row, d.max_seq - 1);
+        cp_async16(ks + swz(row, ch), Kc + (size_t)src_row * kBD + ch * 8);
+        cp_async16(vs + swz(row, ch), Vc + (size_t)src_row * kBD + ch * 8);
+      }
+    };
+#pragma unroll
+    for (int i = 0; i < kBAttnBufs - 1; ++i) {
+      if (cs + i < ce) load(cs + i, i);
+      cp_async_commit();
     }
     {
       const float* qg = d.q + ((size_t)b * kBNQ + 2 * h) * kBD;
@@ -435,114 +453,153 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       qa[kk][1] = g < 2 ? hi1 : lo1;
       if (g >= 4) { qa[kk][0] = 0; qa[kk][1] = 0; }
     }
-    cp_async_wait_all();
-    __syncwarp();
-    // S[16 x 64]: 8 n-tiles of 8 positions
-    float sacc[8][4];
+    // Running softmax state of head g (lanes g < 2): max, denominator, and
+    // the unnormalised output dims 8j + 2tq, +1.
+    float M = -INFINITY, Lsum = 0.f, ro[8][2];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) { sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f; }
+    for (int j = 0; j < 8; ++j) ro[j][0] = ro[j][1] = 0.f;
+#pragma unroll 1
+    for (int c = cs; c < ce; ++c) {
+      const int buf = (c - cs) % kBAttnBufs;
+      // Prefetch chunk c + bufs - 1 into the buffer freed by chunk c - 1,
+      // then wait for chunk c (one commit group per chunk, empty past the
+      // span).
+      if (c + kBAttnBufs - 1 < ce) load(c + kBAttnBufs - 1, (c - cs + kBAttnBufs - 1) % kBAttnBufs);
+      cp_async_commit();
+      cp_async_wait_n<kBAttnBufs - 1>();
+      __syncwarp();
+      const uint32_t ks = smem_u32(sw.k[buf]), vs = smem_u32(sw.v[buf]);
+      const int n = min(kBChunk, p + 1 - c * kBChunk);
+      // S[16 x 64]: 8 n-tiles of 8 positions
+      float sacc[8][4];
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
+      for (int j = 0; j < 8; ++j) { sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f; }
 #pragma unroll
-      for (int jp = 0; jp < 4; ++jp) {
-        // matrices: (n-tile 2jp, k lo), (2jp, k hi), (2jp+1, k lo), (2jp+1, k hi)
-        const int mi = lane >> 3, r = lane & 7;
-        const int row = (2 * jp + (mi >> 1)) * 8 + r, ch = kk * 2 + (mi & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(ks + swz(row, ch), b0, b1, b2, b3);
-        mma_bf16_16816(sacc[2 * jp][0], sacc[2 * jp][1], sacc[2 * jp][2], sacc[2 * jp][3], qa[kk][0], 0u,
-                       qa[kk][1], 0u, b0, b1);
-        mma_bf16_16816(sacc[2 * jp + 1][0], sacc[2 * jp + 1][1], sacc[2 * jp + 1][2], sacc[2 * jp + 1][3],
-                       qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int jp = 0; jp < 4; ++jp) {
+          // matrices: (n-tile 2jp, k lo), (2jp, k hi), (2jp+1, k lo), (2jp+1, k hi)
+          const int mi = lane >> 3, r = lane & 7;
+          const int row = (2 * jp + (mi >> 1)) * 8 + r, ch = kk * 2 + (mi & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(ks + swz(row, ch), b0, b1, b2, b3);
+          mma_bf16_16816(sacc[2 * jp][0], sacc[2 * jp][1], sacc[2 * jp][2], sacc[2 * jp][3], qa[kk][0], 0u,
+                         qa[kk][1], 0u, b0, b1);
+          mma_bf16_16816(sacc[2 * jp + 1][0], sacc[2 * jp + 1][1], sacc[2 * jp + 1][2], sacc[2 * jp + 1][3],
+                         qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+        }
       }
+      // rows 0/1 (+ rows 2/3 from lane + 8): full scores of heads 0/1 in
+      // lanes g = 0 / 1, positions 8j + 2tq, +1
+      float sc[8][2];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float v = sacc[j][e] + __shfl_down_sync(0xffffffffu, sacc[j][e], 8);
+          const int pos = 8 * j + 2 * tq + e;
+          sc[j][e] = pos < n ? v * 0.125f : -INFINITY;
+          mx = fmaxf(mx, sc[j][e]);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      float ls = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          sc[j][e] = expf(sc[j][e] - mx);
+          ls += sc[j][e];
+        }
+      ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+      ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+      // P as A operand: lanes g = 0/1 give hi of their head, lanes g = 2/3 the
+      // lo of lane - 8's probabilities, other rows zero.
+      uint32_t pa[4][2];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int j = 2 * kk + hh;
+          const float p0 = __shfl_up_sync(0xffffffffu, sc[j][0], 8), p1 = __shfl_up_sync(0xffffffffu, sc[j][1], 8);
+          uint32_t hi, lo, hi2, lo2;
+          split2(sc[j][0], sc[j][1], hi, lo);
+          split2(p0, p1, hi2, lo2);
+          pa[kk][hh] = g < 2 ? hi : (g < 4 ? lo2 : 0u);
+        }
+      }
+      // O[16 x 64]: 8 n-tiles of 8 dims, K = positions
+      float oacc[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f; }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int jp = 0; jp < 4; ++jp) {
+          // .trans matrices: (pos lo 8, dims 2jp), (pos hi 8, dims 2jp), (pos lo, 2jp+1), (pos hi, 2jp+1)
+          const int mi = lane >> 3, r = lane & 7;
+          const int row = kk * 16 + (mi & 1) * 8 + r, ch = 2 * jp + (mi >> 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vs + swz(row, ch), b0, b1, b2, b3);
+          mma_bf16_16816(oacc[2 * jp][0], oacc[2 * jp][1], oacc[2 * jp][2], oacc[2 * jp][3], pa[kk][0], 0u,
+                         pa[kk][1], 0u, b0, b1);
+          mma_bf16_16816(oacc[2 * jp + 1][0], oacc[2 * jp + 1][1], oacc[2 * jp + 1][2], oacc[2 * jp + 1][3],
+                         pa[kk][0], 0u, pa[kk][1], 0u, b2, b3);
+        }
+      }
+      // Fold this chunk into the running state (lanes g < 2 hold head g).
+      const float Mn = fmaxf(M, mx);
+      const float ca = expf(M - Mn), cb = expf(mx - Mn);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v0 = oacc[j][0] + __shfl_down_sync(0xffffffffu, oacc[j][0], 8);
+        const float v1 = oacc[j][1] + __shfl_down_sync(0xffffffffu, oacc[j][1], 8);
+        ro[j][0] = ro[j][0] * ca + v0 * cb;
+        ro[j][1] = ro[j][1] * ca + v1 * cb;
+      }
+      Lsum = Lsum * ca + ls * cb;
+      M = Mn;
+      __syncwarp();   // this buffer's readers are done before it is refilled
     }
-    // rows 0/1 (+ rows 2/3 from lane + 8): full scores of heads 0/1 in lanes
-    // g = 0 / 1, positions 8j + 2tq, +1
-    float sc[8][2];
-    float mx = -INFINITY;
+    if (nspan == 1) {
+      // The whole context in one item: normalise and write the outputs.
+      if (g < 2) {
+        const float inv = 1.f / Lsum;
+        const int col = (2 * h + g) * kBD;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float v = sacc[j][e] + __shfl_down_sync(0xffffffffu, sacc[j][e], 8);
-        const int pos = 8 * j + 2 * tq + e;
-        sc[j][e] = pos < n ? v * 0.125f : -INFINITY;
-        mx = fmaxf(mx, sc[j][e]);
+        for (int j = 0; j < 8; ++j) {
+          put_hilo(d.a_att, kBQ, b, col + 8 * j + 2 * tq, ro[j][0] * inv);
+          put_hilo(d.a_att, kBQ, b, col + 8 * j + 2 * tq + 1, ro[j][1] * inv);
+        }
       }
+      continue;
     }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    float ls = 0.f;
+    // Partial {acc[2][64], m[2], l[2]} of span s; the warp that completes
+    // the last span of (b, h) merges them.
+    float* o = d.part + (((size_t)b * kBNKV + h) * d.maxch + s) * 132;
+    if (g < 2) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        sc[j][e] = expf(sc[j][e] - mx);
-        ls += sc[j][e];
-      }
-    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
-    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
-    // P as A operand: lanes g = 0/1 give hi of their head, lanes g = 2/3 the
-    // lo of lane - 8's probabilities, other rows zero.
-    uint32_t pa[4][2];
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int j = 2 * kk + hh;
-        const float p0 = __shfl_up_sync(0xffffffffu, sc[j][0], 8), p1 = __shfl_up_sync(0xffffffffu, sc[j][1], 8);
-        uint32_t hi, lo, hi2, lo2;
-        split2(sc[j][0], sc[j][1], hi, lo);
-        split2(p0, p1, hi2, lo2);
-        pa[kk][hh] = g < 2 ? hi : (g < 4 ? lo2 : 0u);
-      }
-    }
-    // O[16 x 64]: 8 n-tiles of 8 dims, K = positions
-    float oacc[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) { oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f; }
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int jp = 0; jp < 4; ++jp) {
-        // .trans matrices: (pos lo 8, dims 2jp), (pos hi 8, dims 2jp), (pos lo, 2jp+1), (pos hi, 2jp+1)
-        const int mi = lane >> 3, r = lane & 7;
-        const int row = kk * 16 + (mi & 1) * 8 + r, ch = 2 * jp + (mi >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vs + swz(row, ch), b0, b1, b2, b3);
-        mma_bf16_16816(oacc[2 * jp][0], oacc[2 * jp][1], oacc[2 * jp][2], oacc[2 * jp][3], pa[kk][0], 0u,
-                       pa[kk][1], 0u, b0, b1);
-        mma_bf16_16816(oacc[2 * jp + 1][0], oacc[2 * jp + 1][1], oacc[2 * jp + 1][2], oacc[2 * jp + 1][3],
-                       pa[kk][0], 0u, pa[kk][1], 0u, b2, b3);
-      }
-    }
-    // rows 0/1 + rows 2/3: lanes g = 0/1 hold head 0/1, dims 8j + 2tq, +1
-    float* o = d.part + (((size_t)b * kBNKV + h) * d.maxch + c) * 132;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float v0 = oacc[j][0] + __shfl_down_sync(0xffffffffu, oacc[j][0], 8);
-      const float v1 = oacc[j][1] + __shfl_down_sync(0xffffffffu, oacc[j][1], 8);
-      if (g < 2) __stcg(reinterpret_cast<float2*>(o + g * 66 + 8 * j + 2 * tq), make_float2(v0, v1));
+      for (int j = 0; j < 8; ++j) __stcg(reinterpret_cast<float2*>(o + g * 66 + 8 * j + 2 * tq), make_float2(ro[j][0], ro[j][1]));
     }
     if (lane == 0 || lane == 4) {
       const int hh = lane >> 2;
-      __stcg(o + hh * 66 + 64, mx);
-      __stcg(o + hh * 66 + 65, ls);
+      __stcg(o + hh * 66 + 64, M);
+      __stcg(o + hh * 66 + 65, Lsum);
     }
-    // Ticket: the warp finishing the last chunk of (b, h) merges.  The
-    // acq_rel atomic releases this warp's partial stores (ordered before it
-    // by __syncwarp; release is cumulative) and, for the last warp, acquires
-    // every other chunk's.
+    // Ticket: the acq_rel atomic releases this warp's partial stores (ordered
+    // before it by __syncwarp; release is cumulative) and, for the last
+    // warp, acquires every other span's.
     __syncwarp();
     int last = 0;
     if (lane == 0) {
-      const int nc = p / kBChunk + 1;
       const int old = atom_add_acq_rel(d.acnt + b * kBNKV + h, 1);
-      last = old == nc - 1;
+      last = old == nspan - 1;
       if (last) d.acnt[b * kBNKV + h] = 0;
     }
     last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) attn_merge(d, b, h, lane);
+    if (last) attn_merge(d, b, h, lane, nspan);
   }
 }
 
@@ -763,7 +820,13 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
   const CUtensorMap* M = s->maps;
   if (launch_pdl(bembed_kernel, kBMax, 256, 0, st, d, s->wp[0], s->wp[2], forced, prev_out) != cudaSuccess)
     return ::MK_ERR_LAUNCH;
-  const int attn_blocks = s->sms * 3;   // 3 blocks of 4 warps (3 x 66 KB of shared memory) per SM
+  const int attn_blocks = s->sms * kBAttnBlocksPerSm;   // 2-warp blocks, as many as fit per SM
+  // Chunks per attention item: split each (sequence, head) into as many
+  // spans as there are warp slots for all of them at once, at the
+  // engine's capacity; never more items than slots (a second wave of items
+  // would double the layer's attention time).
+  const int per_pair = std::max(1, s->sms * kBAttnBlocksPerSm * kBAttnWarps / (d.batch * kBNKV));
+  const int attn_span = (d.maxch + per_pair - 1) / per_pair;
   static bool attn_attr = false;
   if (!attn_attr) {
     if (cudaFuncSetAttribute(battn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBAttnSmem) != cudaSuccess ||
@@ -777,7 +840,7 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
     if (tc_gemm_launch<EpiQKV>(gemm_params(d, M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, 4),
                                EpiQKV::Params{d, l, s->wp[b + 4], s->wp[b + 5]}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (launch_pdl(battn_kernel, attn_blocks, kBAttnWarps * 32, kBAttnSmem, st, d, l) != cudaSuccess)
+    if (launch_pdl(battn_kernel, attn_blocks, kBAttnWarps * 32, kBAttnSmem, st, d, l, attn_span) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
     if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, 8),
                                  EpiResid::Params{d, d.a_x, s->wp[b + 7]}, s->sms, st) != cudaSuccess)
