@@ -223,6 +223,12 @@ int megakernel_tp_init(void* d_weights, const long long* offsets, int num_offset
 int megakernel_tp_ipc_handle(void* handle, void* out_64_bytes);
 int megakernel_tp_connect(void* handle, const void* handles_tp_size_x_64_bytes);
 int megakernel_tp_info(void* handle, int* rank, int* size);
+/* Check hook for the in-kernel exchange (no reference counterpart): copies
+ * the payloads of this GPU's tensor-parallel exchange slots of the last
+ * layer of the last step -- every rank's partial down projection as it
+ * arrived here over NVLink (own slot written locally) -- into d_out
+ * [tp_size][hidden] fp32 on the engine's device.  Synchronous. */
+int megakernel_tp_exchange_slots(void* handle, float* d_out);
 
 /* ---- host-only helpers (no GPU needed) ----------------------------------- */
 

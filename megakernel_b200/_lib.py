@@ -125,6 +125,7 @@ def signatures() -> dict:
         "megakernel_tp_ipc_handle": ([vp, vp], c_int),
         "megakernel_tp_connect": ([vp, vp], c_int),
         "megakernel_tp_info": ([vp, ip, ip], c_int),
+        "megakernel_tp_exchange_slots": ([vp, vp], c_int),
         "megakernel_infer_shape": ([llp, c_int], c_int),
         "megakernel_rope_table": ([c_int, ctypes.c_double, c_int, fp, fp], c_int),
         "megakernel_plan_bytes": ([c_int, c_int, c_int, llp], c_int),

@@ -423,6 +423,22 @@ void plan_bytes_t(int N, int p, long long* out) {
 
 }  // namespace
 
+namespace {
+// Payload (low 32 bits) of n tagged words at src with a stride, as fp32.
+__global__ void tp_slots_kernel(const uint64_t* src, int n, int stride, float* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __uint_as_float((uint32_t)src[(size_t)i * stride]);
+}
+template <int TP>
+long long tp_slot_offset(int shape_id, int parity) {
+  switch (shape_id) {
+    case 0: return mk::HopLayout<mk::ShapeD64, TP>::X + (long long)parity * TP * mk::ShapeD64::H * mk::kHopSpread;
+    case 2: return mk::HopLayout<mk::ShapeTiny, TP>::X + (long long)parity * TP * mk::ShapeTiny::H * mk::kHopSpread;
+    default: return -1;
+  }
+}
+}  // namespace
+
 extern "C" {
 
 void megakernel_default_options(mk_options* o) {
@@ -706,6 +722,28 @@ int megakernel_tp_connect(void* handle, const void* handles) {
     st->peer_opened[j] = true;
   }
   st->tp_connected = true;
+  return MK_OK;
+}
+
+
+int megakernel_tp_exchange_slots(void* handle, float* d_out) {
+  State* st = as_state(handle);
+  if (!st || !d_out || st->tp_size < 2) return MK_ERR_INVALID_ARG;
+  const ShapeInfo s = shape_info(st->shape_id);
+  // The last layer (L - 1) of a step writes the slots of parity L & 1.
+  const int parity = s.L & 1;
+  long long off = -1;
+  switch (st->tp_size) {
+    case 2: off = tp_slot_offset<2>(st->shape_id, parity); break;
+    case 4: off = tp_slot_offset<4>(st->shape_id, parity); break;
+    case 8: off = tp_slot_offset<8>(st->shape_id, parity); break;
+  }
+  if (off < 0) return set_err(st, MK_ERR_INVALID_ARG);
+  MK_CUDA(cudaSetDevice(st->device));
+  const int n = st->tp_size * s.H;
+  tp_slots_kernel<<<(n + 255) / 256, 256, 0, st->stream>>>(st->d_hop + off, n, mk::kHopSpread, d_out);
+  MK_CUDA(cudaGetLastError());
+  MK_CUDA(cudaStreamSynchronize(st->stream));
   return MK_OK;
 }
 

@@ -4,7 +4,10 @@ Two spawned ranks, one per GPU, exchange CUDA IPC handles over NCCL's
 host-side object gather and then decode with the MLP and LM-head rows split;
 the kernels exchange partial sums and argmax pairs over NVLink.  Checked on
 rank 0 against the golden vectors of the reference's fp32 forward, with the
-same gates as the single-GPU parity tests, and for agreement between ranks.
+same gates as the single-GPU parity tests, for agreement between ranks, and
+against NCCL: the partial sums that arrived over NVLink equal the ones NCCL
+gathers, their sum NCCL's all_reduce, and the in-kernel argmax the argmax of
+the logits NCCL gathers.
 Skipped on a box with fewer than 2 GPUs.
 """
 import os
@@ -49,6 +52,22 @@ def _worker(rank, world, port, out):
         lg = torch.zeros(n, shape.vocab, dtype=torch.float32, device=dev)
         eng.decode_n(toks, n, o, logits=lg)
         full = tp.gather_logits(lg, shape.vocab).cpu().numpy()
+        # Cross-check of the in-kernel NVLink exchange with NCCL: the partial
+        # down projections of the last layer as they arrived in this GPU's
+        # exchange slots equal every rank's own partial gathered by NCCL, and
+        # their rank-order sum equals NCCL's all_reduce of the partials.
+        slots = torch.zeros(world, shape.hidden, dtype=torch.float32, device=dev)
+        assert eng.lib.megakernel_tp_exchange_slots(eng._handle, slots.data_ptr()) == 0
+        own = slots[rank].clone()
+        gathered = [torch.zeros_like(own) for _ in range(world)]
+        dist.all_gather(gathered, own)
+        red = own.clone()
+        dist.all_reduce(red)
+        slots_equal_nccl = all(bool(torch.equal(slots[j], gathered[j])) for j in range(world))
+        ssum = slots[0].clone()
+        for j in range(1, world):
+            ssum += slots[j]
+        sum_err = float((ssum - red).abs().max() / red.abs().max().clamp_min(1e-30))
         allo = [torch.zeros_like(o) for _ in range(world)]
         dist.all_gather(allo, o)
         # free-running greedy from the prompt
@@ -76,7 +95,8 @@ def _worker(rank, world, port, out):
                 full_argmax_ok=bool(np.array_equal(full.argmax(1), o.cpu().numpy())),
                 ranks_agree=all(bool(torch.equal(a, allo[0])) for a in allo),
                 greedy_ok=bool(np.array_equal(got[:upto], want[:upto])),
-                tp_equals_single_gpu=bool(torch.equal(fr, fr1)))
+                tp_equals_single_gpu=bool(torch.equal(fr, fr1)),
+                slots_equal_nccl=slots_equal_nccl, slot_sum_vs_allreduce=sum_err)
         eng.close()
     if rank == 0:
         out.update(res)
@@ -93,3 +113,4 @@ def test_tensor_parallel_vs_reference_2gpu():
         assert r["err"] < LOGIT_TOL, (name, r)
         assert r["argmax_ok"] and r["full_argmax_ok"] and r["ranks_agree"], (name, r)
         assert r["greedy_ok"] and r["tp_equals_single_gpu"], (name, r)
+        assert r["slots_equal_nccl"] and r["slot_sum_vs_allreduce"] < 1e-6, (name, r)
