@@ -188,6 +188,14 @@ int megakernel_prefill(void* handle, const int* d_tokens, int n_tokens, int* d_n
  * Positions start at 0; every step advances every sequence by one. */
 void* megakernel_batch_init(const void* d_weights, const long long* offsets, int num_offsets, int batch,
                             int max_seq);
+/* As megakernel_batch_init with a KV-cache element type (no reference
+ * counterpart): MK_KV_BF16 (the reference's layout) or MK_KV_FP8_E4M3, the
+ * same [batch][L][2][KVH][max_seq][head_dim] layout in e4m3 bytes (half the
+ * cache bytes; K/V rounded to nearest, saturating; attention then runs in
+ * f16 on the tensor cores).  NULL on failure or an unknown type. */
+enum { MK_KV_BF16 = 0, MK_KV_FP8_E4M3 = 1 };
+void* megakernel_batch_init_ex(const void* d_weights, const long long* offsets, int num_offsets, int batch,
+                               int max_seq, int kv_dtype);
 void megakernel_batch_free(void* handle);
 int megakernel_batch_size(void* handle);
 /* One step: d_tokens[batch] (device) -> d_out[batch] next greedy tokens;

@@ -111,6 +111,7 @@ def signatures() -> dict:
         "megakernel_tc_gemm_test": ([vp, c_int, vp, c_int, c_int, vp, vp], c_int),
         "megakernel_prefill": ([vp, vp, c_int, vp, vp], c_int),
         "megakernel_batch_init": ([vp, llp, c_int, c_int, c_int], vp),
+        "megakernel_batch_init_ex": ([vp, llp, c_int, c_int, c_int, c_int], vp),
         "megakernel_batch_free": ([vp], None),
         "megakernel_batch_size": ([vp], c_int),
         "megakernel_batch_step": ([vp, vp, vp, vp, vp], c_int),

@@ -21,7 +21,12 @@ from .weights import offsets_list
 
 
 class BatchDecoder:
-    def __init__(self, flat, offsets, batch, max_seq, shape=QWEN3_0_6B_D64, device=0, lib_path=None):
+    KV_DTYPES = {"bf16": 0, "fp8": 1}
+
+    def __init__(self, flat, offsets, batch, max_seq, shape=QWEN3_0_6B_D64, device=0, lib_path=None,
+                 kv_dtype="bf16"):
+        """kv_dtype: "bf16" (the reference's cache format) or "fp8" (e4m3,
+        half the cache bytes; see megakernel_batch_init_ex)."""
         if shape.name != QWEN3_0_6B_D64.name:
             raise ValueError("the batched path supports the head_dim-64 / intermediate-2816 shape only")
         self.lib = _lib.load(lib_path)
@@ -36,8 +41,9 @@ class BatchDecoder:
             self._weights = torch.from_numpy(np.asarray(flat, dtype=np.uint8)).to(self.device)
         ol = offsets_list(shape, offsets)
         arr = (ctypes.c_longlong * len(ol))(*ol)
-        self._handle = self.lib.megakernel_batch_init(ctypes.c_void_p(self._weights.data_ptr()), arr, len(ol),
-                                                      self.batch, self.max_seq)
+        self.kv_dtype = kv_dtype
+        self._handle = self.lib.megakernel_batch_init_ex(ctypes.c_void_p(self._weights.data_ptr()), arr, len(ol),
+                                                         self.batch, self.max_seq, self.KV_DTYPES[kv_dtype])
         if not self._handle:
             raise RuntimeError("megakernel_batch_init failed (shape, alignment, batch <= 64 or memory)")
         self.vocab = shape.vocab
@@ -71,16 +77,20 @@ class BatchDecoder:
         return list(arr)
 
     def kv_cache(self):
-        """bf16 view [batch, layers, 2, kv_heads, max_seq, head_dim] of the cache (zero copy)."""
+        """View [batch, layers, 2, kv_heads, max_seq, head_dim] of the cache
+        (zero copy): bf16, or float8_e4m3fn with an fp8 cache."""
         s = self.shape
         shape = (self.batch, s.layers, 2, s.kv_heads, self.max_seq, s.head_dim)
         ptr = self.lib.megakernel_batch_kv_ptr(self._handle)
         n = int(np.prod(shape))
+        fp8 = self.kv_dtype == "fp8"
 
         class _Holder:
-            __cuda_array_interface__ = {"shape": (n,), "typestr": "<i2", "data": (ptr, False), "version": 3}
+            __cuda_array_interface__ = {"shape": (n,), "typestr": "|u1" if fp8 else "<i2", "data": (ptr, False),
+                                        "version": 3}
 
-        return torch.as_tensor(_Holder(), device=self.device).view(torch.bfloat16).view(*shape)
+        t = torch.as_tensor(_Holder(), device=self.device)
+        return t.view(torch.float8_e4m3fn if fp8 else torch.bfloat16).view(*shape)
 
     # ---- decoding -----------------------------------------------------------
     def step(self, tokens, logits=False, stream=None):

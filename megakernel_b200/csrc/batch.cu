@@ -7,6 +7,8 @@
 #include <cstdio>
 #include <vector>
 
+#include <cuda_fp16.h>
+
 #include "../../include/megakernel.h"
 #include "tc_gemm.cuh"
 
@@ -64,7 +66,8 @@ struct BatchDev {
   float* q;              // [64][16][64] normed + roped queries
   float* part;           // attention partials [64][8][maxch][2][66]
   unsigned long long* lm_part;  // [2374][64] packed (orderable value, index)
-  __nv_bfloat16* kv;     // [64][L][2][8][max_seq][64]
+  __nv_bfloat16* kv;     // [64][L][2][8][max_seq][64] bf16 cache (nullptr with an fp8 cache)
+  uint8_t* kv8;          // same layout, e4m3 (nullptr with a bf16 cache)
   const float* rope_cos; // [max_seq][32]
   const float* rope_sin;
   int* pos;              // [64] position of each sequence's next token
@@ -79,6 +82,18 @@ struct BatchDev {
 __device__ __forceinline__ size_t bkv_index(const BatchDev& d, int b, int l, int kv, int h, int p) {
   const size_t sq = d.seq_mode ? 0 : (size_t)b;
   return ((((sq * kBL + l) * 2 + kv) * kBNKV + h) * (size_t)d.max_seq + p) * kBD;
+}
+// Two e4m3 values (low byte first) -> two f16 (exact), and two fp32 -> e4m3
+// (round to nearest, saturating).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
+  return r;
+}
+__device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 // 1 / rms of row `seq` of x from the 16 tile partials (fixed order).
 __device__ __forceinline__ float inv_rms(const float* ssq, int seq) {
@@ -169,6 +184,20 @@ struct EpiQKV {
       for (int c = 0; c < 64; c += 4) *reinterpret_cast<float4*>(o + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
     } else {
       const int kv = t < 24 ? 0 : 1, h = t < 24 ? t - 16 : t - 24;
+      if (d.kv8 != nullptr) {
+        // fp8 cache: e4m3, round to nearest, saturating (|K|, |V| << 448).
+        uint8_t* o8 = d.kv8 + bkv_index(d, seq, ep.l, kv, h, p);
+#pragma unroll
+        for (int c = 0; c < 64; c += 16) {
+          uint4 w;
+          w.x = (uint32_t)f32x2_to_e4m3x2(v[c], v[c + 1]) | ((uint32_t)f32x2_to_e4m3x2(v[c + 2], v[c + 3]) << 16);
+          w.y = (uint32_t)f32x2_to_e4m3x2(v[c + 4], v[c + 5]) | ((uint32_t)f32x2_to_e4m3x2(v[c + 6], v[c + 7]) << 16);
+          w.z = (uint32_t)f32x2_to_e4m3x2(v[c + 8], v[c + 9]) | ((uint32_t)f32x2_to_e4m3x2(v[c + 10], v[c + 11]) << 16);
+          w.w = (uint32_t)f32x2_to_e4m3x2(v[c + 12], v[c + 13]) | ((uint32_t)f32x2_to_e4m3x2(v[c + 14], v[c + 15]) << 16);
+          *reinterpret_cast<uint4*>(o8 + c) = w;
+        }
+        return;
+      }
       __nv_bfloat16* o = d.kv + bkv_index(d, seq, ep.l, kv, h, p);
 #pragma unroll
       for (int c = 0; c < 64; c += 8) {
@@ -298,12 +327,20 @@ constexpr int kBAttnWarps = 2;
 #endif
 constexpr int kBAttnBufs = MK_BATTN_BUFS;   // chunks of K/V per warp: current + in flight
 constexpr int kBAttnBlocksPerSm = kBAttnBufs == 2 ? 3 : 2;
-struct AttnWarpSmem {
-  alignas(128) __nv_bfloat16 k[kBAttnBufs][kBChunk * kBD];  // 8 KB each, swizzled
-  alignas(128) __nv_bfloat16 v[kBAttnBufs][kBChunk * kBD];
+// bf16 cache: K/V chunks land swizzled in kBAttnBufs buffers.  fp8 cache
+// (e4m3): the chunks land unswizzled in kBAttnBufs staging buffers (4 KB
+// each) and are converted into one f16 working tile (swizzled) before use.
+template <bool F8>
+struct AttnWarpSmemT {
+  static constexpr int kTiles = F8 ? 1 : kBAttnBufs;
+  alignas(128) uint16_t k[kTiles][kBChunk * kBD];  // 8 KB each, swizzled (bf16 or f16)
+  alignas(128) uint16_t v[kTiles][kBChunk * kBD];
+  alignas(128) uint8_t k8[F8 ? kBAttnBufs : 1][F8 ? kBChunk * kBD : 16];   // fp8 staging
+  alignas(128) uint8_t v8[F8 ? kBAttnBufs : 1][F8 ? kBChunk * kBD : 16];
   alignas(16) float q[2][kBD];
 };
-constexpr size_t kBAttnSmem = sizeof(AttnWarpSmem) * kBAttnWarps;
+template <bool F8>
+constexpr size_t attn_smem_bytes() { return sizeof(AttnWarpSmemT<F8>) * kBAttnWarps; }
 
 __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   int old;
@@ -333,6 +370,34 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
   const __nv_bfloat16 ha = __float2bfloat16_rn(a), hb = __float2bfloat16_rn(b);
   hi = pack_bf16x2(__bfloat162float(ha), __bfloat162float(hb));
   lo = pack_bf16x2(a - __bfloat162float(ha), b - __bfloat162float(hb));
+}
+
+// f16 counterparts for the fp8-cache attention (e4m3 converts to f16
+// exactly; all operands of one mma share a type).
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <bool F16>
+__device__ __forceinline__ void split2t(float a, float b, uint32_t& hi, uint32_t& lo) {
+  if constexpr (F16) {
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    hi = pack_f16x2(__half2float(ha), __half2float(hb));
+    lo = pack_f16x2(a - __half2float(ha), b - __half2float(hb));
+  } else {
+    split2(a, b, hi, lo);
+  }
+}
+template <bool F16>
+__device__ __forceinline__ void mmat(float& d0, float& d1, float& d2, float& d3, uint32_t a0, uint32_t a1,
+                                     uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (F16)
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    mma_bf16_16816(d0, d1, d2, d3, a0, a1, a2, a3, b0, b1);
 }
 
 // Merge of the chunk partials of (b, h) for both query heads: lanes load the
@@ -394,11 +459,12 @@ __device__ __forceinline__ void attn_merge(const BatchDev& d, int b, int h, int 
   }
 }
 
+template <bool F8>
 __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int l, int span) {
   extern __shared__ __align__(128) uint8_t attn_smem_raw[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int g = lane >> 2, tq = lane & 3;
-  AttnWarpSmem& sw = reinterpret_cast<AttnWarpSmem*>(attn_smem_raw)[wid];
+  AttnWarpSmemT<F8>& sw = reinterpret_cast<AttnWarpSmemT<F8>*>(attn_smem_raw)[wid];
   const int wglob = blockIdx.x * kBAttnWarps + wid;
   const int nw = gridDim.x * kBAttnWarps;
   const int maxspan = (d.maxch + span - 1) / span;
@@ -414,19 +480,30 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
     if (cs >= nc) continue;
     const int ce = min(nc, cs + span);
     const int nspan = (nc + span - 1) / span;
-    const __nv_bfloat16* Kc = d.kv + bkv_index(d, b, l, 0, h, 0);
-    const __nv_bfloat16* Vc = d.kv + bkv_index(d, b, l, 1, h, 0);
+    const size_t k_off = bkv_index(d, b, l, 0, h, 0), v_off = bkv_index(d, b, l, 1, h, 0);
     __syncwarp();   // the previous item's readers of sw are done
-    // K and V of chunk c (64 rows x 8 chunks of 16 B each) into buffer `buf`;
-    // rows past max_seq clamp (masked later).
+    // K and V of chunk c into buffer `buf`: bf16, 64 rows x 8 pieces of 16 B
+    // swizzled; fp8, 64 rows x 4 pieces of 16 B plain.  Rows past max_seq
+    // clamp (masked later).
     auto load = [&](int c, int buf) {
-      const uint32_t ks = smem_u32(sw.k[buf]), vs = smem_u32(sw.v[buf]);
+      if constexpr (F8) {
+        const uint32_t ks = smem_u32(sw.k8[buf]), vs = smem_u32(sw.v8[buf]);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const int idx = lane + 32 * k, row = idx >> 3, ch = idx & 7;
-        const int src_row = min(c * kBChunk + row, d.max_seq - 1);
-        cp_async16(ks + swz(row, ch), Kc + (size_t)src_row * kBD + ch * 8);
-        cp_async16(vs + swz(row, ch), Vc + (size_t)src_row * kBD + ch * 8);
+        for (int k = 0; k < 8; ++k) {
+          const int idx = lane + 32 * k, row = idx >> 2, ch = idx & 3;
+          const size_t src_row = (size_t)min(c * kBChunk + row, d.max_seq - 1);
+          cp_async16(ks + (uint32_t)(row * 64 + ch * 16), d.kv8 + k_off + src_row * kBD + ch * 16);
+          cp_async16(vs + (uint32_t)(row * 64 + ch * 16), d.kv8 + v_off + src_row * kBD + ch * 16);
+        }
+      } else {
+        const uint32_t ks = smem_u32(sw.k[buf]), vs = smem_u32(sw.v[buf]);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int idx = lane + 32 * k, row = idx >> 3, ch = idx & 7;
+          const size_t src_row = (size_t)min(c * kBChunk + row, d.max_seq - 1);
+          cp_async16(ks + swz(row, ch), d.kv + k_off + src_row * kBD + ch * 8);
+          cp_async16(vs + swz(row, ch), d.kv + v_off + src_row * kBD + ch * 8);
+        }
       }
     };
 #pragma unroll
@@ -446,8 +523,8 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       uint32_t hi0 = 0, lo0 = 0, hi1 = 0, lo1 = 0;
       if (g < 4) {
         const float* qr = &sw.q[g & 1][kk * 16 + 2 * tq];
-        split2(qr[0], qr[1], hi0, lo0);
-        split2(qr[8], qr[9], hi1, lo1);
+        split2t<F8>(qr[0], qr[1], hi0, lo0);
+        split2t<F8>(qr[8], qr[9], hi1, lo1);
       }
       qa[kk][0] = g < 2 ? hi0 : lo0;
       qa[kk][1] = g < 2 ? hi1 : lo1;
@@ -468,7 +545,25 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       cp_async_commit();
       cp_async_wait_n<kBAttnBufs - 1>();
       __syncwarp();
-      const uint32_t ks = smem_u32(sw.k[buf]), vs = smem_u32(sw.v[buf]);
+      if constexpr (F8) {
+        // e4m3 -> f16 (exact) into the swizzled working tile.
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int idx = lane + 32 * k, row = idx >> 3, ch = idx & 7;
+          const uint2 ka = *reinterpret_cast<const uint2*>(&sw.k8[buf][row * 64 + ch * 8]);
+          const uint2 va = *reinterpret_cast<const uint2*>(&sw.v8[buf][row * 64 + ch * 8]);
+          uint4 ko, vo;
+          ko.x = e4m3x2_to_f16x2((uint16_t)ka.x); ko.y = e4m3x2_to_f16x2((uint16_t)(ka.x >> 16));
+          ko.z = e4m3x2_to_f16x2((uint16_t)ka.y); ko.w = e4m3x2_to_f16x2((uint16_t)(ka.y >> 16));
+          vo.x = e4m3x2_to_f16x2((uint16_t)va.x); vo.y = e4m3x2_to_f16x2((uint16_t)(va.x >> 16));
+          vo.z = e4m3x2_to_f16x2((uint16_t)va.y); vo.w = e4m3x2_to_f16x2((uint16_t)(va.y >> 16));
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sw.k[0]) + swz(row, ch)) = ko;
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sw.v[0]) + swz(row, ch)) = vo;
+        }
+        __syncwarp();
+      }
+      const int tb = F8 ? 0 : buf;
+      const uint32_t ks = smem_u32(sw.k[tb]), vs = smem_u32(sw.v[tb]);
       const int n = min(kBChunk, p + 1 - c * kBChunk);
       // S[16 x 64]: 8 n-tiles of 8 positions
       float sacc[8][4];
@@ -483,9 +578,9 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
           const int row = (2 * jp + (mi >> 1)) * 8 + r, ch = kk * 2 + (mi & 1);
           uint32_t b0, b1, b2, b3;
           ldsm_x4(ks + swz(row, ch), b0, b1, b2, b3);
-          mma_bf16_16816(sacc[2 * jp][0], sacc[2 * jp][1], sacc[2 * jp][2], sacc[2 * jp][3], qa[kk][0], 0u,
+          mmat<F8>(sacc[2 * jp][0], sacc[2 * jp][1], sacc[2 * jp][2], sacc[2 * jp][3], qa[kk][0], 0u,
                          qa[kk][1], 0u, b0, b1);
-          mma_bf16_16816(sacc[2 * jp + 1][0], sacc[2 * jp + 1][1], sacc[2 * jp + 1][2], sacc[2 * jp + 1][3],
+          mmat<F8>(sacc[2 * jp + 1][0], sacc[2 * jp + 1][1], sacc[2 * jp + 1][2], sacc[2 * jp + 1][3],
                          qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
         }
       }
@@ -525,8 +620,8 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
           const int j = 2 * kk + hh;
           const float p0 = __shfl_up_sync(0xffffffffu, sc[j][0], 8), p1 = __shfl_up_sync(0xffffffffu, sc[j][1], 8);
           uint32_t hi, lo, hi2, lo2;
-          split2(sc[j][0], sc[j][1], hi, lo);
-          split2(p0, p1, hi2, lo2);
+          split2t<F8>(sc[j][0], sc[j][1], hi, lo);
+          split2t<F8>(p0, p1, hi2, lo2);
           pa[kk][hh] = g < 2 ? hi : (g < 4 ? lo2 : 0u);
         }
       }
@@ -543,9 +638,9 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
           const int row = kk * 16 + (mi & 1) * 8 + r, ch = 2 * jp + (mi >> 1);
           uint32_t b0, b1, b2, b3;
           ldsm_x4_t(vs + swz(row, ch), b0, b1, b2, b3);
-          mma_bf16_16816(oacc[2 * jp][0], oacc[2 * jp][1], oacc[2 * jp][2], oacc[2 * jp][3], pa[kk][0], 0u,
+          mmat<F8>(oacc[2 * jp][0], oacc[2 * jp][1], oacc[2 * jp][2], oacc[2 * jp][3], pa[kk][0], 0u,
                          pa[kk][1], 0u, b0, b1);
-          mma_bf16_16816(oacc[2 * jp + 1][0], oacc[2 * jp + 1][1], oacc[2 * jp + 1][2], oacc[2 * jp + 1][3],
+          mmat<F8>(oacc[2 * jp + 1][0], oacc[2 * jp + 1][1], oacc[2 * jp + 1][2], oacc[2 * jp + 1][3],
                          pa[kk][0], 0u, pa[kk][1], 0u, b2, b3);
         }
       }
@@ -708,7 +803,7 @@ void batch_free(BatchState* s) {
   if (!s) return;
   cudaFree(s->d.x); cudaFree(s->d.ssq); cudaFree(s->d.a_x); cudaFree(s->d.a_att); cudaFree(s->d.a_h);
   cudaFree(s->d.q); cudaFree(s->d.part); cudaFree(s->d.lm_part);
-  if (s->owns_kv) cudaFree(s->d.kv);
+  if (s->owns_kv) { cudaFree(s->d.kv); cudaFree(s->d.kv8); }
   cudaFree(s->d_tmp);
   cudaFree(const_cast<float*>(s->d.rope_cos)); cudaFree(const_cast<float*>(s->d.rope_sin));
   cudaFree(s->d.pos); cudaFree(s->d.err); cudaFree(s->maps); cudaFree(s->d.ws); cudaFree(s->d.tickets); cudaFree(s->d.acnt);
@@ -722,10 +817,11 @@ bool balloc(T** p, size_t bytes) {
 
 // ext_kv: bind to a caller-owned cache of one sequence ([L][2][KVH][max_seq][hd])
 // instead of allocating [batch] caches (used by the parallel prefill).
+// kv_fp8: keep the cache in e4m3 (half the bytes; own cache only).
 BatchState* batch_init(const void* d_weights, const long long* offsets, int num_offsets, int batch, int max_seq,
-                       __nv_bfloat16* ext_kv = nullptr) {
+                       __nv_bfloat16* ext_kv = nullptr, bool kv_fp8 = false) {
   using namespace mk;
-  if (!d_weights || !offsets || batch < 1 || batch > kBMax || max_seq < 1) return nullptr;
+  if (!d_weights || !offsets || batch < 1 || batch > kBMax || max_seq < 1 || (kv_fp8 && ext_kv)) return nullptr;
   if (infer_shape(offsets, num_offsets) != 0) return nullptr;   // d64 shape only
   for (int i = 0; i < num_offsets; ++i)
     if (offsets[i] < 0 || (offsets[i] & 15) != 0) return nullptr;
@@ -750,7 +846,7 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
   d.batch = batch;
   d.max_seq = max_seq;
   d.maxch = (max_seq + kBChunk - 1) / kBChunk;
-  s->kv_bytes = ext_kv ? 0 : (long long)batch * kBL * 2 * kBNKV * (long long)max_seq * kBD * 2;
+  s->kv_bytes = ext_kv ? 0 : (long long)batch * kBL * 2 * kBNKV * (long long)max_seq * kBD * (kv_fp8 ? 1 : 2);
   s->owns_kv = ext_kv == nullptr;
   float *rc = nullptr, *rs = nullptr;
   const bool ok =
@@ -759,7 +855,8 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
       balloc(&d.q, sizeof(float) * kBMax * kBNQ * kBD) &&
       balloc(&d.part, sizeof(float) * (size_t)kBMax * kBNKV * d.maxch * 132) &&
       balloc(&d.lm_part, sizeof(unsigned long long) * (size_t)kBLMTiles * kBMax) &&
-      (ext_kv ? (d.kv = ext_kv) != nullptr : balloc(&d.kv, (size_t)s->kv_bytes)) &&
+      (ext_kv ? (d.kv = ext_kv) != nullptr
+              : (kv_fp8 ? balloc(&d.kv8, (size_t)s->kv_bytes) : balloc(&d.kv, (size_t)s->kv_bytes))) &&
       balloc(&s->d_tmp, sizeof(int) * kBMax) && balloc(&rc, sizeof(float) * (size_t)max_seq * 32) &&
       balloc(&rs, sizeof(float) * (size_t)max_seq * 32) && balloc(&d.pos, sizeof(int) * kBMax) &&
       balloc(&d.err, sizeof(int) * 4) && balloc(&s->maps, sizeof(CUtensorMap) * (map_lm() + 1)) &&
@@ -829,18 +926,25 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
   const int attn_span = (d.maxch + per_pair - 1) / per_pair;
   static bool attn_attr = false;
   if (!attn_attr) {
-    if (cudaFuncSetAttribute(battn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBAttnSmem) != cudaSuccess ||
-        cudaFuncSetAttribute(battn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    if (cudaFuncSetAttribute(battn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn_smem_bytes<false>()) != cudaSuccess ||
+        cudaFuncSetAttribute(battn_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess ||
+        cudaFuncSetAttribute(battn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn_smem_bytes<true>()) != cudaSuccess ||
+        cudaFuncSetAttribute(battn_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
     attn_attr = true;
   }
+  const bool f8 = d.kv8 != nullptr;
   for (int l = 0; l < kBL; ++l) {
     const int b = 2 + 11 * l;
     const __nv_bfloat16* g_next = l + 1 < kBL ? s->wp[b + 11] : s->wp[1];
     if (tc_gemm_launch<EpiQKV>(gemm_params(d, M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, 4),
                                EpiQKV::Params{d, l, s->wp[b + 4], s->wp[b + 5]}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (launch_pdl(battn_kernel, attn_blocks, kBAttnWarps * 32, kBAttnSmem, st, d, l, attn_span) != cudaSuccess)
+    if ((f8 ? launch_pdl(battn_kernel<true>, attn_blocks, kBAttnWarps * 32, attn_smem_bytes<true>(), st, d, l, attn_span)
+            : launch_pdl(battn_kernel<false>, attn_blocks, kBAttnWarps * 32, attn_smem_bytes<false>(), st, d, l,
+                         attn_span)) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
     if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, 8),
                                  EpiResid::Params{d, d.a_x, s->wp[b + 7]}, s->sms, st) != cudaSuccess)
@@ -933,6 +1037,12 @@ void* megakernel_batch_init(const void* d_weights, const long long* offsets, int
   return batch_init(d_weights, offsets, num_offsets, batch, max_seq);
 }
 
+void* megakernel_batch_init_ex(const void* d_weights, const long long* offsets, int num_offsets, int batch,
+                               int max_seq, int kv_dtype) {
+  if (kv_dtype != MK_KV_BF16 && kv_dtype != MK_KV_FP8_E4M3) return nullptr;
+  return batch_init(d_weights, offsets, num_offsets, batch, max_seq, nullptr, kv_dtype == MK_KV_FP8_E4M3);
+}
+
 void megakernel_batch_free(void* handle) {
   if (!handle) return;
   cudaDeviceSynchronize();
@@ -978,7 +1088,11 @@ int megakernel_batch_get_pos(void* handle, int* h_pos) {
                                                                                                    : MK_ERR_CUDA;
 }
 
-void* megakernel_batch_kv_ptr(void* handle) { return handle ? static_cast<BatchState*>(handle)->d.kv : nullptr; }
+void* megakernel_batch_kv_ptr(void* handle) {
+  if (!handle) return nullptr;
+  const BatchState* s = static_cast<BatchState*>(handle);
+  return s->d.kv8 ? static_cast<void*>(s->d.kv8) : static_cast<void*>(s->d.kv);
+}
 
 long long megakernel_batch_kv_bytes(void* handle) {
   return handle ? static_cast<BatchState*>(handle)->kv_bytes : 0;

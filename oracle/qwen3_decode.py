@@ -25,7 +25,9 @@ step below follows that module for one new token with an explicit KV cache:
 ``kv_bf16=True`` rounds K (after RoPE) and V to bf16 before they are cached and
 used, which is what the kernel does: its KV cache is bf16
 (src/kv_cache.cuh:9-32 layout ``[layer, 2, kv_head, max_seq, head_dim]``).  With
-``kv_bf16=False`` it is the plain HF fp32 forward.
+``kv_bf16=False`` it is the plain HF fp32 forward.  ``kv_fp8=True`` rounds
+them to float8 e4m3 instead (round to nearest, saturating at +-448), the
+batched decoder's optional fp8 cache.
 
 Parity pin: tests/test_oracle_pin.py checks this module against golden logits
 that tests/golden/make_golden.py produced by running the reference's own
@@ -51,9 +53,10 @@ class Qwen3DecodeOracle:
     """Token-serial fp32 decode over bf16-valued weights with an explicit KV cache."""
 
     def __init__(self, shape, weights: dict, kv_bf16: bool = True,
-                 max_seq: int = 2048, device: str = "cpu"):
+                 max_seq: int = 2048, device: str = "cpu", kv_fp8: bool = False):
         self.s = shape
         self.kv_bf16 = kv_bf16
+        self.kv_fp8 = kv_fp8
         self.dev = torch.device(device)
         f = lambda n: weights[n].to(self.dev).float()  # noqa: E731
         self.emb = f("embedding")
@@ -111,7 +114,10 @@ class Qwen3DecodeOracle:
             k = self._rms(k, w["k_norm"])
             q = self._rope(q, p)
             k = self._rope(k, p)
-            if self.kv_bf16:
+            if self.kv_fp8:
+                k = k.clamp(-448, 448).to(torch.float8_e4m3fn).float()
+                v = v.clamp(-448, 448).to(torch.float8_e4m3fn).float()
+            elif self.kv_bf16:
                 k = k.to(torch.bfloat16).float()
                 v = v.to(torch.bfloat16).float()
             self.k[li, :, p] = k

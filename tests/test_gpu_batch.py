@@ -105,3 +105,36 @@ def test_batch_long_context_configs3_vs_oracle():
         assert err < LOGIT_TOL, (b, err)
         ok = om[P:] > MARGIN
         assert np.array_equal(out[b][ok], ot[P:][ok])
+
+
+def test_batch_fp8_kv_cache_vs_oracle():
+    """The batched decoder with an e4m3 KV cache (megakernel_batch_init_ex):
+    against the fp32 oracle that rounds K/V to e4m3 the same way -- the
+    north-star logit gate and argmax where the margin > 1e-2 -- and, for the
+    record, the error against the bf16-cache oracle (the reference's cache
+    precision), which must stay below the documented 0.5 bound."""
+    shape, w, flat, offs = weights("qwen3-0.6b-d64")
+    B, P, S = 8, 200, 3
+    toks = _tokens(B, P + S, seed=13)
+    bd = BatchDecoder(flat, offs, batch=B, max_seq=P + S + 16, kv_dtype="fp8")
+    assert bd.kv_cache().dtype == torch.float8_e4m3fn
+    bd.decode_n(toks[:, :P].t().contiguous().to(DEV, torch.int32), P)
+    lgs, outs = [], []
+    for t in range(P, P + S):
+        out, lg = bd.step(toks[:, t].to(DEV), logits=True)
+        lgs.append(lg.cpu().numpy())
+        outs.append(out.cpu().numpy())
+    lg, out = np.stack(lgs, 1), np.stack(outs, 1)
+    bd.close()
+    for b in (0, 5):
+        o8 = Qwen3DecodeOracle(shape, w, kv_fp8=True, max_seq=P + S + 8, device="cuda")
+        ot, ol, om = o8.run(toks[b].tolist(), P + S)
+        err = np.abs(lg[b] - ol[P:]).max()
+        assert err < LOGIT_TOL, (b, err)
+        ok = om[P:] > MARGIN
+        assert np.array_equal(out[b][ok], ot[P:][ok])
+        o16 = Qwen3DecodeOracle(shape, w, kv_bf16=True, max_seq=P + S + 8, device="cuda")
+        _, ol16, _ = o16.run(toks[b].tolist(), P + S)
+        err16 = np.abs(lg[b] - ol16[P:]).max()
+        print(f"fp8 KV, sequence {b}: max |logit - e4m3 oracle| {err:.2e}, vs bf16-cache oracle {err16:.2e}")
+        assert err16 < 0.5, err16
