@@ -5,6 +5,7 @@
 // split of fp32 activations into the 128-row bf16 A operand, and a test entry
 // point that runs one tcgen05 GEMM with a plain epilogue.
 #include <cstdio>
+#include <cstdlib>
 #include <vector>
 
 #include <cuda_fp16.h>
@@ -936,23 +937,29 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
     attn_attr = true;
   }
   const bool f8 = d.kv8 != nullptr;
+  // Split-K factors of the q/k/v, O, gate/up and down GEMMs.  Measured on
+  // B200 (64 sequences at position 1024, ms per step): {4, 8, 1, 8} 3.21,
+  // {2, 4, 1, 4} 2.83, {1, 1, 1, 1} 2.92, {1, 2, 1, 3} 2.72 -- the split-K
+  // fixup (partials through L2, a ticket, the last CTA summing them) costs
+  // more than the extra CTAs save.
+  constexpr int ks[4] = {1, 2, 1, 3};
   for (int l = 0; l < kBL; ++l) {
     const int b = 2 + 11 * l;
     const __nv_bfloat16* g_next = l + 1 < kBL ? s->wp[b + 11] : s->wp[1];
-    if (tc_gemm_launch<EpiQKV>(gemm_params(d, M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, 4),
+    if (tc_gemm_launch<EpiQKV>(gemm_params(d, M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, ks[0]),
                                EpiQKV::Params{d, l, s->wp[b + 4], s->wp[b + 5]}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
     if ((f8 ? launch_pdl(battn_kernel<true>, attn_blocks, kBAttnWarps * 32, attn_smem_bytes<true>(), st, d, l, attn_span)
             : launch_pdl(battn_kernel<false>, attn_blocks, kBAttnWarps * 32, attn_smem_bytes<false>(), st, d, l,
                          attn_span)) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, 8),
+    if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, ks[1]),
                                  EpiResid::Params{d, d.a_x, s->wp[b + 7]}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (tc_gemm_launch<EpiSwiGLU>(gemm_params(d, M + kMapAx, M + map_layer(l, 2), kBH, kBI / 32, kBI, 1),
+    if (tc_gemm_launch<EpiSwiGLU>(gemm_params(d, M + kMapAx, M + map_layer(l, 2), kBH, kBI / 32, kBI, ks[2]),
                                   EpiSwiGLU::Params{d}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAh, M + map_layer(l, 3), kBI, kBH / 64, 0, 8),
+    if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAh, M + map_layer(l, 3), kBI, kBH / 64, 0, ks[3]),
                                  EpiResid::Params{d, d.a_x, g_next}, s->sms, st) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
   }
