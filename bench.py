@@ -296,6 +296,7 @@ def run_ours(args, world, rank, local):
         line["long_context"] = run_long(shape, flat, offs, dev, peak)
         line["batched"] = run_batched(shape, flat, offs, dev, peak)
         line["batched_fp8_kv"] = run_batched(shape, flat, offs, dev, peak, kv_dtype="fp8")
+        line["batched_fp8_weights"] = run_batched(shape, flat, offs, dev, peak, w_dtype="fp8")
     if rank == 0:
         print(json.dumps(line), flush=True)
     eng.close()
@@ -376,14 +377,14 @@ def run_long(shape, flat, offs, dev, peak):
                          "algorithmic_bytes": bytes_total}}
 
 
-def run_batched(shape, flat, offs, dev, peak, kv_dtype="bf16"):
+def run_batched(shape, flat, offs, dev, peak, kv_dtype="bf16", w_dtype="bf16"):
     """BASELINE.json configs[3] on the batched path (rank 0, N=1): 64 sequences,
     1024-token random prompts (seed 1 + sequence index) prefilled through the
     batched decode itself (teacher-forced, untimed), then 256 greedy steps timed
     with CUDA events.  Reported beside the headline, not as it."""
     from megakernel_b200.batch import BatchDecoder
     B, P, G = 64, 1024, 256
-    bd = BatchDecoder(flat, offs, batch=B, max_seq=P + G + 16, kv_dtype=kv_dtype)
+    bd = BatchDecoder(flat, offs, batch=B, max_seq=P + G + 16, kv_dtype=kv_dtype, w_dtype=w_dtype)
     prompts = torch.stack([torch.randint(0, shape.vocab, (P,), generator=torch.Generator().manual_seed(1 + b))
                            for b in range(B)], 1).to(dev, torch.int32)          # [P, B]
     pre = bd.decode_n(prompts, P)                 # prefill through the batched step itself (untimed, warms up)
@@ -399,13 +400,16 @@ def run_batched(shape, flat, offs, dev, peak, kv_dtype="bf16"):
     ms = e0.elapsed_time(e1)
     p_lo = pos0[0]
     kv = sum(57344 * (p + 2) for p in range(p_lo, p_lo + G)) * B // (2 if kv_dtype == "fp8" else 1)
-    bytes_total = 971_891_712 * G + kv
+    # e4m3: GEMM matrices + per-row scales + bf16 norms + 64 embedding rows
+    bytes_total = (971_891_712 if w_dtype == "bf16" else 487_836_160) * G + kv
     bd.close()
     return {
         "workload": "configs[3]: 64 sequences x (1024-token random prompt + 256 greedy tokens), Qwen3-0.6B d64"
                     + (", e4m3 KV cache (logits within 2e-2 of an e4m3-cache fp32 oracle, ~0.24 of the bf16-cache one)"
-                       if kv_dtype == "fp8" else ""),
-        "kv_dtype": kv_dtype,
+                       if kv_dtype == "fp8" else "")
+                    + (", e4m3 GEMM weights with per-row scales (logits within 3e-3 of an e4m3-weight fp32 oracle, "
+                       "~0.55 of the bf16 model)" if w_dtype == "fp8" else ""),
+        "kv_dtype": kv_dtype, "w_dtype": w_dtype,
         "value": B * G / (ms / 1e3), "unit": "tok/s (aggregate over 64 sequences)", "ms_per_step": ms / G,
         "steps": G, "positions": [p_lo, p_lo + G - 1],
         "roofline": {"bound": "hbm", "achieved": bytes_total / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",

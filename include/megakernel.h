@@ -169,6 +169,11 @@ int megakernel_decode_noalloc(const void* d_weights, const long long* offsets, i
  * Returns MK_OK or an MK_ERR_* code. */
 int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d_w, int K, int N, float* d_out,
                             void* stream);
+/* The same on e4m3 weights: d_w8 [N][K] e4m3 bytes with per-row scales
+ * d_scale[N] (W = scale * e4m3), through the GEMM's e4m3 -> bf16 converter
+ * warps (the path megakernel_batch_init_ex(..., MK_W_FP8_E4M3) runs). */
+int megakernel_tc_gemm_test_e4m3(const float* d_x, int rows, const void* d_w8, const float* d_scale, int K, int N,
+                                 float* d_out, void* stream);
 
 /* Parallel prefill (no reference counterpart; replaces the token-serial
  * prompt loop of host/bridge.py:158-162): feeds d_tokens[n_tokens] (device)
@@ -188,14 +193,20 @@ int megakernel_prefill(void* handle, const int* d_tokens, int n_tokens, int* d_n
  * Positions start at 0; every step advances every sequence by one. */
 void* megakernel_batch_init(const void* d_weights, const long long* offsets, int num_offsets, int batch,
                             int max_seq);
-/* As megakernel_batch_init with a KV-cache element type (no reference
- * counterpart): MK_KV_BF16 (the reference's layout) or MK_KV_FP8_E4M3, the
- * same [batch][L][2][KVH][max_seq][head_dim] layout in e4m3 bytes (half the
- * cache bytes; K/V rounded to nearest, saturating; attention then runs in
- * f16 on the tensor cores).  NULL on failure or an unknown type. */
-enum { MK_KV_BF16 = 0, MK_KV_FP8_E4M3 = 1 };
+/* As megakernel_batch_init with storage options (no reference counterpart),
+ * `flags` a combination of:
+ *   MK_KV_FP8_E4M3  the KV cache in e4m3 -- the same [batch][L][2][KVH]
+ *                   [max_seq][head_dim] layout in bytes (half the cache;
+ *                   K/V rounded to nearest, saturating; attention then runs
+ *                   in f16 on the tensor cores);
+ *   MK_W_FP8_E4M3   the GEMMs on an e4m3 copy of the weights made at init
+ *                   (one scale per row, max |w| / 448; half the weight
+ *                   bytes; the caller's bf16 weights stay in use for the
+ *                   embedding and the norms).
+ * MK_KV_BF16 (0) is the reference's precision.  NULL on failure. */
+enum { MK_KV_BF16 = 0, MK_KV_FP8_E4M3 = 1, MK_W_FP8_E4M3 = 2 };
 void* megakernel_batch_init_ex(const void* d_weights, const long long* offsets, int num_offsets, int batch,
-                               int max_seq, int kv_dtype);
+                               int max_seq, int flags);
 void megakernel_batch_free(void* handle);
 int megakernel_batch_size(void* handle);
 /* One step: d_tokens[batch] (device) -> d_out[batch] next greedy tokens;

@@ -22,11 +22,14 @@ from .weights import offsets_list
 
 class BatchDecoder:
     KV_DTYPES = {"bf16": 0, "fp8": 1}
+    W_DTYPES = {"bf16": 0, "fp8": 2}
 
     def __init__(self, flat, offsets, batch, max_seq, shape=QWEN3_0_6B_D64, device=0, lib_path=None,
-                 kv_dtype="bf16"):
+                 kv_dtype="bf16", w_dtype="bf16"):
         """kv_dtype: "bf16" (the reference's cache format) or "fp8" (e4m3,
-        half the cache bytes; see megakernel_batch_init_ex)."""
+        half the cache bytes); w_dtype: "bf16" or "fp8" (the GEMMs on an
+        e4m3 copy of the weights with per-row scales).  See
+        megakernel_batch_init_ex."""
         if shape.name != QWEN3_0_6B_D64.name:
             raise ValueError("the batched path supports the head_dim-64 / intermediate-2816 shape only")
         self.lib = _lib.load(lib_path)
@@ -41,9 +44,10 @@ class BatchDecoder:
             self._weights = torch.from_numpy(np.asarray(flat, dtype=np.uint8)).to(self.device)
         ol = offsets_list(shape, offsets)
         arr = (ctypes.c_longlong * len(ol))(*ol)
-        self.kv_dtype = kv_dtype
+        self.kv_dtype, self.w_dtype = kv_dtype, w_dtype
+        flags = self.KV_DTYPES[kv_dtype] | self.W_DTYPES[w_dtype]
         self._handle = self.lib.megakernel_batch_init_ex(ctypes.c_void_p(self._weights.data_ptr()), arr, len(ol),
-                                                         self.batch, self.max_seq, self.KV_DTYPES[kv_dtype])
+                                                         self.batch, self.max_seq, flags)
         if not self._handle:
             raise RuntimeError("megakernel_batch_init failed (shape, alignment, batch <= 64 or memory)")
         self.vocab = shape.vocab

@@ -768,6 +768,50 @@ extern "C" int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d
   return rc;
 }
 
+// The same GEMM on e4m3 weights: d_w8 [N][K] e4m3 bytes, d_scale [N] per-row
+// scales (W = scale * e4m3); the converter-warp path of the batched GEMMs.
+extern "C" int megakernel_tc_gemm_test_e4m3(const float* d_x, int rows, const void* d_w8, const float* d_scale,
+                                             int K, int N, float* d_out, void* stream) {
+  if (!d_x || !d_w8 || !d_scale || !d_out || rows < 1 || rows > 64 || K < 64 || K % 64 != 0 || N < 64 ||
+      N % 64 != 0)
+    return MK_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return MK_ERR_CUDA;
+  __nv_bfloat16* a = nullptr;
+  CUtensorMap* maps = nullptr;
+  int* err = nullptr;
+  int rc = MK_OK;
+  if (cudaMalloc(&a, (size_t)128 * K * 2) != cudaSuccess || cudaMalloc(&maps, 2 * sizeof(CUtensorMap)) != cudaSuccess ||
+      cudaMalloc(&err, sizeof(int)) != cudaSuccess) {
+    rc = MK_ERR_OOM;
+  } else {
+    CUtensorMap h[2];
+    if (!mk::tc_make_map(&h[0], a, 128, (uint64_t)K, 128) ||
+        !mk::tc_make_map_e4m3(&h[1], d_w8, (uint64_t)N, (uint64_t)K, 32)) {
+      rc = MK_ERR_INVALID_ARG;
+    } else {
+      cudaMemcpyAsync(maps, h, sizeof(h), cudaMemcpyHostToDevice, st);
+      cudaMemsetAsync(err, 0, sizeof(int), st);
+      mk::hilo_split_kernel<<<64, 256, 0, st>>>(d_x, rows, K, a);
+      mk::TcGemmParams p{maps, maps + 1, K, N / 64, 0, err, 1000000000LL, 1, nullptr, nullptr, d_scale};
+      mk::EpiStore::Params ep{d_out, N, rows};
+      if (mk::tc_gemm_launch<mk::EpiStore, true>(p, ep, sms, st) != cudaSuccess) rc = MK_ERR_LAUNCH;
+      int herr = 0;
+      if (cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+          cudaStreamSynchronize(st) != cudaSuccess)
+        rc = MK_ERR_CUDA;
+      else if (rc == MK_OK)
+        rc = herr;
+    }
+  }
+  cudaFree(a);
+  cudaFree(maps);
+  cudaFree(err);
+  return rc;
+}
+
 // ============================================================================
 // Batched decode: host side.
 // ============================================================================
@@ -782,7 +826,45 @@ struct BatchState {
   long long kv_bytes = 0;
   bool owns_kv = true;
   int* d_tmp = nullptr;          // [64] scratch tokens (prefill)
+  // e4m3 weights (optional): per layer the q|k|v, O, gate|up and down
+  // matrices, then the LM head, each row scaled by its own factor.
+  uint8_t* w8 = nullptr;
+  float* wsc = nullptr;
+  size_t w8_off[4 * mk::kBL + 1] = {};
+  size_t sc_off[4 * mk::kBL + 1] = {};
 };
+
+// Rows x cols of the matrix behind GEMM map k of a layer (0 q|k|v, 1 O,
+// 2 gate|up, 3 down; 4: the LM head).
+inline void gemm_matrix(int k, int& rows, int& cols) {
+  using namespace mk;
+  switch (k) {
+    case 0: rows = kBQ + 2 * kBKV; cols = kBH; break;
+    case 1: rows = kBH; cols = kBQ; break;
+    case 2: rows = 2 * kBI; cols = kBH; break;
+    case 3: rows = kBH; cols = kBI; break;
+    default: rows = kBV; cols = kBH; break;
+  }
+}
+
+// e4m3 copy of a bf16 matrix with one scale per row (max |w| / 448): one
+// warp per row.
+__global__ void quant_rows_kernel(const __nv_bfloat16* __restrict__ w, int rows, int cols, uint8_t* __restrict__ q,
+                                  float* __restrict__ scale) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const __nv_bfloat16* wr = w + (size_t)row * cols;
+  float amax = 0.f;
+  for (int c = lane; c < cols; c += 32) amax = fmaxf(amax, fabsf(__bfloat162float(wr[c])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float sc = amax > 0.f ? amax / 448.f : 1.f;
+  const float inv = 1.f / sc;
+  uint16_t* qr = reinterpret_cast<uint16_t*>(q + (size_t)row * cols);
+  for (int c = 2 * lane; c < cols; c += 64)
+    qr[c >> 1] = mk::f32x2_to_e4m3x2(__bfloat162float(wr[c]) * inv, __bfloat162float(wr[c + 1]) * inv);
+  if (lane == 0) scale[row] = sc;
+}
 
 enum { kMapAx = 0, kMapAatt = 1, kMapAh = 2, kMapLayer0 = 3 };
 constexpr size_t kBWsBytes = (size_t)2 << 20;
@@ -805,6 +887,8 @@ void batch_free(BatchState* s) {
   cudaFree(s->d.x); cudaFree(s->d.ssq); cudaFree(s->d.a_x); cudaFree(s->d.a_att); cudaFree(s->d.a_h);
   cudaFree(s->d.q); cudaFree(s->d.part); cudaFree(s->d.lm_part);
   if (s->owns_kv) { cudaFree(s->d.kv); cudaFree(s->d.kv8); }
+  cudaFree(s->w8);
+  cudaFree(s->wsc);
   cudaFree(s->d_tmp);
   cudaFree(const_cast<float*>(s->d.rope_cos)); cudaFree(const_cast<float*>(s->d.rope_sin));
   cudaFree(s->d.pos); cudaFree(s->d.err); cudaFree(s->maps); cudaFree(s->d.ws); cudaFree(s->d.tickets); cudaFree(s->d.acnt);
@@ -819,8 +903,9 @@ bool balloc(T** p, size_t bytes) {
 // ext_kv: bind to a caller-owned cache of one sequence ([L][2][KVH][max_seq][hd])
 // instead of allocating [batch] caches (used by the parallel prefill).
 // kv_fp8: keep the cache in e4m3 (half the bytes; own cache only).
+// w_fp8: run the GEMMs on an e4m3 copy of the weights (per-row scales).
 BatchState* batch_init(const void* d_weights, const long long* offsets, int num_offsets, int batch, int max_seq,
-                       __nv_bfloat16* ext_kv = nullptr, bool kv_fp8 = false) {
+                       __nv_bfloat16* ext_kv = nullptr, bool kv_fp8 = false, bool w_fp8 = false) {
   using namespace mk;
   if (!d_weights || !offsets || batch < 1 || batch > kBMax || max_seq < 1 || (kv_fp8 && ext_kv)) return nullptr;
   if (infer_shape(offsets, num_offsets) != 0) return nullptr;   // d64 shape only
@@ -886,6 +971,30 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
           tc_make_map(&h[map_layer(l, 3)], s->wp[b + 10], kBH, kBI, 32);
   }
   mok = mok && tc_make_map(&h[map_lm()], s->wp[0], kBV, kBH, 32);
+  if (mok && w_fp8) {
+    // e4m3 copies of the GEMM weights; their maps replace the bf16 ones.
+    size_t wo = 0, so = 0;
+    for (int m = 0; m <= 4 * kBL; ++m) {
+      int rows, cols;
+      gemm_matrix(m == 4 * kBL ? 4 : m % 4, rows, cols);
+      s->w8_off[m] = wo;
+      s->sc_off[m] = so;
+      wo += (size_t)rows * cols;
+      so += (size_t)rows;
+    }
+    mok = balloc(&s->w8, wo) && balloc(&s->wsc, so * sizeof(float));
+    for (int m = 0; m <= 4 * kBL && mok; ++m) {
+      const int k = m == 4 * kBL ? 4 : m % 4, l = m / 4;
+      int rows, cols;
+      gemm_matrix(k, rows, cols);
+      const int wkey = k == 0 ? 1 : (k == 1 ? 6 : (k == 2 ? 8 : 10));
+      const __nv_bfloat16* src = k == 4 ? s->wp[0] : s->wp[2 + 11 * l + wkey];
+      quant_rows_kernel<<<(rows + 7) / 8, 256>>>(src, rows, cols, s->w8 + s->w8_off[m], s->wsc + s->sc_off[m]);
+      mok = cudaGetLastError() == cudaSuccess &&
+            tc_make_map_e4m3(&h[k == 4 ? map_lm() : map_layer(l, k)], s->w8 + s->w8_off[m], rows, cols, 32);
+    }
+    mok = mok && cudaDeviceSynchronize() == cudaSuccess;
+  }
   if (!mok || cudaMemcpy(s->maps, h.data(), sizeof(CUtensorMap) * h.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
     batch_free(s);
     return nullptr;
@@ -911,6 +1020,9 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), int grid, int block, size_t sme
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
+
+template <class T>
+struct Tag { using type = T; };
 
 int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, float* logits, cudaStream_t st) {
   using namespace mk;
@@ -943,28 +1055,37 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
   // fixup (partials through L2, a ticket, the last CTA summing them) costs
   // more than the extra CTAs save.
   constexpr int ks[4] = {1, 2, 1, 3};
+  const bool w8 = s->w8 != nullptr;
+  // GEMM of map slot m (layer l, kind k; m = 4L: LM head) on the bf16 or
+  // the e4m3 weights.
+  auto gemm = [&](auto epi_tag, TcGemmParams p, const auto& ep, int m) -> cudaError_t {
+    using Epi = typename decltype(epi_tag)::type;
+    if (!w8) return tc_gemm_launch<Epi, false>(p, ep, s->sms, st);
+    p.wscale = s->wsc + s->sc_off[m];
+    return tc_gemm_launch<Epi, true>(p, ep, s->sms, st);
+  };
   for (int l = 0; l < kBL; ++l) {
     const int b = 2 + 11 * l;
     const __nv_bfloat16* g_next = l + 1 < kBL ? s->wp[b + 11] : s->wp[1];
-    if (tc_gemm_launch<EpiQKV>(gemm_params(d, M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, ks[0]),
-                               EpiQKV::Params{d, l, s->wp[b + 4], s->wp[b + 5]}, s->sms, st) != cudaSuccess)
+    if (gemm(Tag<EpiQKV>{}, gemm_params(d, M + kMapAx, M + map_layer(l, 0), kBH, (kBQ + 2 * kBKV) / 64, 0, ks[0]),
+             EpiQKV::Params{d, l, s->wp[b + 4], s->wp[b + 5]}, 4 * l) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
     if ((f8 ? launch_pdl(battn_kernel<true>, attn_blocks, kBAttnWarps * 32, attn_smem_bytes<true>(), st, d, l, attn_span)
             : launch_pdl(battn_kernel<false>, attn_blocks, kBAttnWarps * 32, attn_smem_bytes<false>(), st, d, l,
                          attn_span)) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, ks[1]),
-                                 EpiResid::Params{d, d.a_x, s->wp[b + 7]}, s->sms, st) != cudaSuccess)
+    if (gemm(Tag<EpiResid>{}, gemm_params(d, M + kMapAatt, M + map_layer(l, 1), kBQ, kBH / 64, 0, ks[1]),
+             EpiResid::Params{d, d.a_x, s->wp[b + 7]}, 4 * l + 1) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (tc_gemm_launch<EpiSwiGLU>(gemm_params(d, M + kMapAx, M + map_layer(l, 2), kBH, kBI / 32, kBI, ks[2]),
-                                  EpiSwiGLU::Params{d}, s->sms, st) != cudaSuccess)
+    if (gemm(Tag<EpiSwiGLU>{}, gemm_params(d, M + kMapAx, M + map_layer(l, 2), kBH, kBI / 32, kBI, ks[2]),
+             EpiSwiGLU::Params{d}, 4 * l + 2) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
-    if (tc_gemm_launch<EpiResid>(gemm_params(d, M + kMapAh, M + map_layer(l, 3), kBI, kBH / 64, 0, ks[3]),
-                                 EpiResid::Params{d, d.a_x, g_next}, s->sms, st) != cudaSuccess)
+    if (gemm(Tag<EpiResid>{}, gemm_params(d, M + kMapAh, M + map_layer(l, 3), kBI, kBH / 64, 0, ks[3]),
+             EpiResid::Params{d, d.a_x, g_next}, 4 * l + 3) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
   }
-  if (tc_gemm_launch<EpiArgmax>(gemm_params(d, M + kMapAx, M + map_lm(), kBH, kBLMTiles, 0, 1),
-                                EpiArgmax::Params{d, logits}, s->sms, st) != cudaSuccess)
+  if (gemm(Tag<EpiArgmax>{}, gemm_params(d, M + kMapAx, M + map_lm(), kBH, kBLMTiles, 0, 1),
+           EpiArgmax::Params{d, logits}, 4 * kBL) != cudaSuccess)
     return ::MK_ERR_LAUNCH;
   if (launch_pdl(bargmax_kernel, s->batch, 256, 0, st, d, out) != cudaSuccess) return ::MK_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? ::MK_OK : ::MK_ERR_LAUNCH;
@@ -1045,9 +1166,10 @@ void* megakernel_batch_init(const void* d_weights, const long long* offsets, int
 }
 
 void* megakernel_batch_init_ex(const void* d_weights, const long long* offsets, int num_offsets, int batch,
-                               int max_seq, int kv_dtype) {
-  if (kv_dtype != MK_KV_BF16 && kv_dtype != MK_KV_FP8_E4M3) return nullptr;
-  return batch_init(d_weights, offsets, num_offsets, batch, max_seq, nullptr, kv_dtype == MK_KV_FP8_E4M3);
+                               int max_seq, int flags) {
+  if (flags & ~(MK_KV_FP8_E4M3 | MK_W_FP8_E4M3)) return nullptr;
+  return batch_init(d_weights, offsets, num_offsets, batch, max_seq, nullptr, (flags & MK_KV_FP8_E4M3) != 0,
+                    (flags & MK_W_FP8_E4M3) != 0);
 }
 
 void megakernel_batch_free(void* handle) {

@@ -25,6 +25,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cstdint>
 
 #include "../../include/megakernel.h"
@@ -39,6 +40,17 @@ constexpr int kTcStageBytes = kTcABytes + kTcWBytes;  // 24 KB
 constexpr int kTcThreads = 256;
 constexpr int kTcCombStride = 65;                     // floats per row of the hi/lo combine buffer
 constexpr size_t kTcSmemBytes = 1024 + (size_t)kTcStages * kTcStageBytes + 64 * kTcCombStride * 4;
+// Per-instance ring: with e4m3 weights (W8) each stage also holds the 4 KB
+// e4m3 W block that two converter warps expand into the bf16 W tile, and the
+// ring has 7 stages (shared memory).
+template <bool W8>
+struct TcCfg {
+  static constexpr int kStages = W8 ? 7 : kTcStages;
+  static constexpr int kW8Bytes = W8 ? kTcBN * kTcBK : 0;
+  static constexpr int kStageBytes = kTcStageBytes + kW8Bytes;
+  static constexpr uint32_t kTxBytes = W8 ? kTcABytes + kW8Bytes : kTcStageBytes;
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 64 * kTcCombStride * 4;
+};
 constexpr uint32_t kTcTmemCols = 128;                 // two 64-column accumulators
 
 struct TcGemmParams {
@@ -52,6 +64,7 @@ struct TcGemmParams {
   int ksplit;               // K blocks split over this many CTAs per tile (1: no split)
   float* ws;                // split partials [ntiles][ksplit][64][64] (ksplit > 1)
   int* counters;            // [ntiles] arrival tickets, 0 between launches (ksplit > 1)
+  const float* wscale;      // e4m3 weights only: per-W-row scale (the GEMM uses W = scale * e4m3)
 };
 
 // W rows of tile t: [r0, r0+32) then [r1, r1+32).  Plain: 64t and 64t+32;
@@ -80,19 +93,30 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const Tc
   }
 }
 
-template <class Epi>
+// e4m3 pair (low byte first) -> bf16 pair, exactly (through f16).
+__device__ __forceinline__ uint32_t tc_e4m3x2_to_bf16x2(uint16_t v) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v));
+  const __half2 hh = *reinterpret_cast<const __half2*>(&h);
+  const float2 f = __half22float2(hh);
+  const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+
+template <class Epi, bool W8 = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ TcGemmParams p, const __grid_constant__ typename Epi::Params ep) {
+  using C = TcCfg<W8>;
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-  float* comb = reinterpret_cast<float*>(smem + (size_t)kTcStages * kTcStageBytes);
-  __shared__ alignas(8) uint64_t full[kTcStages], empty[kTcStages], tfull[2], tempty[2];
+  float* comb = reinterpret_cast<float*>(smem + (size_t)C::kStages * C::kStageBytes);
+  __shared__ alignas(8) uint64_t full[kTcStages], empty[kTcStages], conv[kTcStages], tfull[2], tempty[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < C::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); mbar_init(&conv[s], 2); }
     for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
     abort_flag = 0;
     fence_mbar_init();
@@ -119,12 +143,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int r0, r1;
       tc_tile_rows(p, t, r0, r1);
       const int kb0 = sp * kper, kb1 = min(kblocks, (sp + 1) * kper);
-      pre = min(kTcStages, kb1 - kb0);
+      pre = min(C::kStages, kb1 - kb0);
       for (int j = 0; j < pre; ++j) {
-        uint8_t* st = smem + (size_t)j * kTcStageBytes;
-        mbar_arrive_expect_tx(&full[j], kTcStageBytes);
-        tma_load_2d(st + kTcABytes, p.wmap, (kb0 + j) * kTcBK, r0, &full[j]);
-        tma_load_2d(st + kTcABytes + kTcWBytes / 2, p.wmap, (kb0 + j) * kTcBK, r1, &full[j]);
+        uint8_t* st = smem + (size_t)j * C::kStageBytes;
+        mbar_arrive_expect_tx(&full[j], C::kTxBytes);
+        // bf16 W: the two 32-row halves of the SW128 tile; e4m3 W: the two
+        // halves of the staging block after the tile (64 bytes per row).
+        uint8_t* wdst = W8 ? st + kTcABytes + kTcWBytes : st + kTcABytes;
+        const int half = W8 ? C::kW8Bytes / 2 : kTcWBytes / 2;
+        tma_load_2d(wdst, p.wmap, (kb0 + j) * kTcBK, r0, &full[j]);
+        tma_load_2d(wdst + half, p.wmap, (kb0 + j) * kTcBK, r1, &full[j]);
       }
     }
     pdl_wait();
@@ -135,17 +163,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int r0, r1;
       tc_tile_rows(p, t, r0, r1);
       for (int kb = sp * kper; kb < min(kblocks, (sp + 1) * kper); ++kb, ++issued) {
-        uint8_t* st = smem + (size_t)s * kTcStageBytes;
+        uint8_t* st = smem + (size_t)s * C::kStageBytes;
         if (issued < pre) {
           tma_load_2d(st, p.amap, kb * kTcBK, 0, &full[s]);
         } else {
           if (!tc_wait(&empty[s], ph ^ 1u, p, &abort_flag)) goto done_producer;
-          mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+          mbar_arrive_expect_tx(&full[s], C::kTxBytes);
           tma_load_2d(st, p.amap, kb * kTcBK, 0, &full[s]);
-          tma_load_2d(st + kTcABytes, p.wmap, kb * kTcBK, r0, &full[s]);
-          tma_load_2d(st + kTcABytes + kTcWBytes / 2, p.wmap, kb * kTcBK, r1, &full[s]);
+          uint8_t* wdst = W8 ? st + kTcABytes + kTcWBytes : st + kTcABytes;
+          const int half = W8 ? C::kW8Bytes / 2 : kTcWBytes / 2;
+          tma_load_2d(wdst, p.wmap, kb * kTcBK, r0, &full[s]);
+          tma_load_2d(wdst + half, p.wmap, kb * kTcBK, r1, &full[s]);
         }
-        if (++s == kTcStages) { s = 0; ph ^= 1u; }
+        if (++s == C::kStages) { s = 0; ph ^= 1u; }
       }
     }
   done_producer:;
@@ -163,18 +193,51 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t d = tmem + (uint32_t)(buf * kTcBN);
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!tc_wait(&full[s], ph, p, &abort_flag)) { ok = false; break; }
+        if (!tc_wait(W8 ? &conv[s] : &full[s], ph, p, &abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t a = smem_u32(smem + (size_t)s * kTcStageBytes);
+        const uint32_t a = smem_u32(smem + (size_t)s * C::kStageBytes);
         const uint32_t w = a + kTcABytes;
 #pragma unroll
         for (int kk = 0; kk < kTcBK / 16; ++kk)
           tc_mma_bf16(d, tc_desc_sw128(a + kk * 32), tc_desc_sw128(w + kk * 32), idesc, (kb > kb0) || kk != 0);
         tc_commit(&empty[s]);
-        if (++s == kTcStages) { s = 0; ph ^= 1u; }
+        if (++s == C::kStages) { s = 0; ph ^= 1u; }
       }
       if (!ok) break;
       tc_commit(&tfull[buf]);
+    }
+  } else if (W8 && (warp == 2 || warp == 3)) {
+    // ---- e4m3 -> bf16 converter (W8 only) ----
+    // Each lane expands one W row of the stage's e4m3 block (64 bytes) into
+    // the 128-byte-swizzled bf16 tile the MMA reads, then the warp makes its
+    // writes visible to the tensor core (async proxy) and arrives on conv.
+    const int row = 32 * (warp - 2) + lane;
+    uint32_t s = 0, ph = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+      const int sp = u % p.ksplit;
+      const int kb0 = sp * kper, kb1 = min(kblocks, (sp + 1) * kper);
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!tc_wait(&full[s], ph, p, &abort_flag)) { ok = false; break; }
+        uint8_t* st = smem + (size_t)s * C::kStageBytes;
+        const uint8_t* src = st + kTcABytes + kTcWBytes + row * 64;
+        uint8_t* dst = st + kTcABytes + row * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint2 w = *reinterpret_cast<const uint2*>(src + 8 * j);
+          uint4 o;
+          o.x = tc_e4m3x2_to_bf16x2((uint16_t)w.x);
+          o.y = tc_e4m3x2_to_bf16x2((uint16_t)(w.x >> 16));
+          o.z = tc_e4m3x2_to_bf16x2((uint16_t)w.y);
+          o.w = tc_e4m3x2_to_bf16x2((uint16_t)(w.y >> 16));
+          *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) = o;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[s]);
+        if (++s == C::kStages) { s = 0; ph ^= 1u; }
+      }
+      if (!ok) break;
     }
   } else if (warp >= 4) {
     // ---- epilogue ----
@@ -247,6 +310,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (q < 2 && do_epi) {
+        if constexpr (W8) {
+          // W = scale * e4m3: column c of the tile is W row r0 + c (c < 32)
+          // or r1 + c - 32.
+          int r0, r1;
+          tc_tile_rows(p, t, r0, r1);
+#pragma unroll
+          for (int c = 0; c < 64; ++c) v[c] *= __ldg(p.wscale + (c < 32 ? r0 + c : r1 + c - 32));
+        }
         Epi::apply(ep, t, row, v);
         // Column phase: the row values go through shared memory so that
         // global writes are coalesced (lanes = consecutive columns).
@@ -301,13 +372,27 @@ inline bool tc_make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <class Epi>
+// Row-major e4m3 matrix [rows x cols] (bytes) -> tensor map with a {64, box_rows}
+// box, no swizzle (the converter warps swizzle while expanding to bf16).
+inline bool tc_make_map_e4m3(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  PFN_encodeTiled enc = tc_encode_fn();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols % 16 != 0) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <class Epi, bool W8 = false>
 inline cudaError_t tc_gemm_launch(const TcGemmParams& p, const typename Epi::Params& ep, int max_ctas,
                                   cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kTcSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<Epi, W8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)TcCfg<W8>::kSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
@@ -316,14 +401,14 @@ inline cudaError_t tc_gemm_launch(const TcGemmParams& p, const typename Epi::Par
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = kTcSmemBytes;
+  cfg.dynamicSmemBytes = TcCfg<W8>::kSmem;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Epi>, p, ep);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Epi, W8>, p, ep);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -27,7 +27,10 @@ used, which is what the kernel does: its KV cache is bf16
 (src/kv_cache.cuh:9-32 layout ``[layer, 2, kv_head, max_seq, head_dim]``).  With
 ``kv_bf16=False`` it is the plain HF fp32 forward.  ``kv_fp8=True`` rounds
 them to float8 e4m3 instead (round to nearest, saturating at +-448), the
-batched decoder's optional fp8 cache.
+batched decoder's optional fp8 cache.  ``w_fp8=True`` runs the matrix
+products on e4m3 weights with one scale per row (max |w| / 448), as the
+batched decoder's optional e4m3 weights do; the embedding lookup and the
+norms keep the bf16 weights.
 
 Parity pin: tests/test_oracle_pin.py checks this module against golden logits
 that tests/golden/make_golden.py produced by running the reference's own
@@ -49,21 +52,35 @@ def rope_tables(head_dim: int, theta: float, positions: int):
     return freqs.cos(), freqs.sin()
 
 
+def quant_rows_e4m3(w: torch.Tensor) -> torch.Tensor:
+    """w with each row rounded to e4m3 at its own scale (max |row| / 448), dequantised to fp32."""
+    amax = w.abs().amax(dim=1, keepdim=True)
+    sc = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    inv = 1.0 / sc            # the kernel scales by the fp32 reciprocal, then rounds
+    return (w * inv).clamp(-448, 448).to(torch.float8_e4m3fn).float() * sc
+
+
 class Qwen3DecodeOracle:
     """Token-serial fp32 decode over bf16-valued weights with an explicit KV cache."""
 
     def __init__(self, shape, weights: dict, kv_bf16: bool = True,
-                 max_seq: int = 2048, device: str = "cpu", kv_fp8: bool = False):
+                 max_seq: int = 2048, device: str = "cpu", kv_fp8: bool = False, w_fp8: bool = False):
         self.s = shape
         self.kv_bf16 = kv_bf16
         self.kv_fp8 = kv_fp8
         self.dev = torch.device(device)
         f = lambda n: weights[n].to(self.dev).float()  # noqa: E731
+        # e4m3 rounding is done on the CPU (torch's CUDA cast rounded some
+        # values differently from the CPU cast and the kernel's cvt.rn).
+        q = lambda n: quant_rows_e4m3(weights[n].float()).to(self.dev)  # noqa: E731
         self.emb = f("embedding")
+        self.lm = q("embedding") if w_fp8 else self.emb
         self.final_norm = f("final_norm")
         self.layers = []
+        gemm_keys = {"w_q", "w_k", "w_v", "w_o", "w_gate", "w_up", "w_down"}
         for i in range(shape.layers):
-            self.layers.append({k: f(f"layer.{i}.{k}") for k in shape.LAYER_KEYS})
+            self.layers.append({k: (q(f"layer.{i}.{k}") if w_fp8 and k in gemm_keys else f(f"layer.{i}.{k}"))
+                                for k in shape.LAYER_KEYS})
         self.max_seq = max_seq
         self.cos, self.sin = rope_tables(shape.head_dim, shape.rope_theta, max_seq)
         self.cos, self.sin = self.cos.to(self.dev), self.sin.to(self.dev)
@@ -115,8 +132,9 @@ class Qwen3DecodeOracle:
             q = self._rope(q, p)
             k = self._rope(k, p)
             if self.kv_fp8:
-                k = k.clamp(-448, 448).to(torch.float8_e4m3fn).float()
-                v = v.clamp(-448, 448).to(torch.float8_e4m3fn).float()
+                # rounded on the CPU, like the weights (see __init__)
+                k = k.cpu().clamp(-448, 448).to(torch.float8_e4m3fn).float().to(self.dev)
+                v = v.cpu().clamp(-448, 448).to(torch.float8_e4m3fn).float().to(self.dev)
             elif self.kv_bf16:
                 k = k.to(torch.bfloat16).float()
                 v = v.to(torch.bfloat16).float()
@@ -136,7 +154,7 @@ class Qwen3DecodeOracle:
             x = x + w["w_down"] @ (torch.nn.functional.silu(g) * u)
         h = self._rms(x, self.final_norm)
         self.pos += 1
-        return self.emb @ h
+        return self.lm @ h
 
     def run(self, forced: list[int], n_steps: int, want_logits: bool = True):
         """Teacher-forced for len(forced) steps then greedy; mirrors megakernel_decode_n.

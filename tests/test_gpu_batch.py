@@ -138,3 +138,35 @@ def test_batch_fp8_kv_cache_vs_oracle():
         err16 = np.abs(lg[b] - ol16[P:]).max()
         print(f"fp8 KV, sequence {b}: max |logit - e4m3 oracle| {err:.2e}, vs bf16-cache oracle {err16:.2e}")
         assert err16 < 0.5, err16
+
+
+def test_batch_fp8_weights_vs_oracle():
+    """The batched decoder on e4m3 weights (per-row scales; the tcgen05 GEMMs
+    expand each e4m3 W block to bf16 in shared memory): against the fp32
+    oracle with the same weight rounding -- the north-star logit gate and
+    argmax where the margin > 1e-2 -- and, for the record, against the bf16
+    model (documented bound 1.0)."""
+    shape, w, flat, offs = weights("qwen3-0.6b-d64")
+    B, P, S = 4, 40, 3
+    toks = _tokens(B, P + S, seed=17)
+    bd = BatchDecoder(flat, offs, batch=B, max_seq=P + S + 16, w_dtype="fp8")
+    bd.decode_n(toks[:, :P].t().contiguous().to(DEV, torch.int32), P)
+    lgs, outs = [], []
+    for t in range(P, P + S):
+        out, lg = bd.step(toks[:, t].to(DEV), logits=True)
+        lgs.append(lg.cpu().numpy())
+        outs.append(out.cpu().numpy())
+    lg, out = np.stack(lgs, 1), np.stack(outs, 1)
+    bd.close()
+    for b in (0, 3):
+        o8 = Qwen3DecodeOracle(shape, w, kv_bf16=True, max_seq=P + S + 8, device="cuda", w_fp8=True)
+        ot, ol, om = o8.run(toks[b].tolist(), P + S)
+        err = np.abs(lg[b] - ol[P:]).max()
+        assert err < LOGIT_TOL, (b, err)
+        ok = om[P:] > MARGIN
+        assert np.array_equal(out[b][ok], ot[P:][ok])
+        o16 = Qwen3DecodeOracle(shape, w, kv_bf16=True, max_seq=P + S + 8, device="cuda")
+        _, ol16, _ = o16.run(toks[b].tolist(), P + S)
+        err16 = np.abs(lg[b] - ol16[P:]).max()
+        print(f"fp8 weights, sequence {b}: max |logit - e4m3-weight oracle| {err:.2e}, vs bf16 model {err16:.2e}")
+        assert err16 < 1.0, err16

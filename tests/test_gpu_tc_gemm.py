@@ -29,3 +29,25 @@ def test_tc_gemm_matches_fp64(rows, K, N):
     ref = x.double() @ w.double().t()
     err = ((out.double() - ref).abs().max() / ref.abs().max()).item()
     assert err < 2e-5, err
+
+
+@pytest.mark.parametrize("rows,K,N", [(64, 1024, 2048), (64, 2816, 1024), (5, 1024, 256)])
+def test_tc_gemm_e4m3_weights_match_fp64(rows, K, N):
+    """The e4m3-weight form (converter warps expand each W block to bf16 in
+    shared memory; per-row scales in the epilogue) against x @ (s * q)^T in
+    fp64 with the same e4m3 values."""
+    L = _lib.load()
+    g = torch.Generator(device="cpu").manual_seed(rows + K + 3 * N)
+    x = torch.randn(rows, K, generator=g).to(DEV)
+    w = torch.randn(N, K, generator=g) * 0.02
+    sc = w.abs().amax(dim=1) / 448.0
+    q = (w / sc[:, None]).to(torch.float8_e4m3fn)
+    q_dev, sc_dev = q.view(torch.uint8).to(DEV), sc.to(DEV)
+    out = torch.zeros(rows, N, device=DEV)
+    rc = L.megakernel_tc_gemm_test_e4m3(ctypes.c_void_p(x.data_ptr()), rows, ctypes.c_void_p(q_dev.data_ptr()),
+                                        ctypes.c_void_p(sc_dev.data_ptr()), K, N, ctypes.c_void_p(out.data_ptr()),
+                                        None)
+    assert rc == 0, rc
+    ref = x.double() @ (q.double() * sc.double()[:, None]).t().to(DEV)
+    err = ((out.double() - ref).abs().max() / ref.abs().max()).item()
+    assert err < 2e-5, err
