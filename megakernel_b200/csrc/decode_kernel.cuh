@@ -61,7 +61,7 @@
 #endif
 // Pause between polling rounds of a tagged-word wait (ns).
 #ifndef MK_POLL_BACKOFF_NS
-#define MK_POLL_BACKOFF_NS 200
+#define MK_POLL_BACKOFF_NS 50
 #endif
 
 namespace mk {
