@@ -12,7 +12,7 @@ from megakernel_b200.shapes import QWEN3_0_6B_D64, QWEN3_0_6B_D128, TINY
 
 @pytest.mark.parametrize("shape", [TINY, QWEN3_0_6B_D64, QWEN3_0_6B_D128])
 def test_sizes(shape):
-    # 971,891,712 B for the graded shape (SURVEY 8d), 1,192,099,840 B for d128.
+    # 971,891,712 B for the graded shape, 1,192,099,840 B for d128.
     want = {"tiny": None, "qwen3-0.6b-d64": 971891712, "qwen3-0.6b-d128": 1192099840}[shape.name]
     if want:
         assert shape.weight_bytes == want
