@@ -1158,6 +1158,13 @@ extern "C" int megakernel_prefill(void* handle, const int* d_tokens, int n_token
   return set_err(st, rc);
 }
 
+#if MK_TC_STAMPS
+// Profiling build only: copies the GEMM stamps [256][64] (u64 ns) to host.
+extern "C" int megakernel_tc_stamps(void* h_out) {
+  return cudaMemcpyFromSymbol(h_out, mk::g_tc_stamps, sizeof(mk::g_tc_stamps)) == cudaSuccess ? 0 : -2;
+}
+#endif
+
 extern "C" {
 
 void* megakernel_batch_init(const void* d_weights, const long long* offsets, int num_offsets, int batch,

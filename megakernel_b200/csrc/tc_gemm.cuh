@@ -93,6 +93,22 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const Tc
   }
 }
 
+// Profiling build only (-DMK_TC_STAMPS=1): %globaltimer stamps of the
+// down-projection launches (K = 2816) per CTA, read back with
+// megakernel_tc_stamps; the last such launch of a step remains.
+#ifndef MK_TC_STAMPS
+#define MK_TC_STAMPS 0
+#endif
+#if MK_TC_STAMPS
+__device__ unsigned long long g_tc_stamps[256][64];
+#define TC_STAMP(k)                                                                  \
+  do {                                                                              \
+    if (p.K == 2816 && blockIdx.x < 256) g_tc_stamps[blockIdx.x][(k)] = globaltimer_ns(); \
+  } while (0)
+#else
+#define TC_STAMP(k) do {} while (0)
+#endif
+
 // e4m3 pair (low byte first) -> bf16 pair, exactly (through f16).
 __device__ __forceinline__ uint32_t tc_e4m3x2_to_bf16x2(uint16_t v) {
   uint32_t h;
@@ -132,6 +148,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int kper = (kblocks + p.ksplit - 1) / p.ksplit;   // K blocks per split
   const int nunits = p.ntiles * p.ksplit;
 
+  if (threadIdx.x == 0) TC_STAMP(0);
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
     // Weights do not depend on the previous kernel: the W blocks of the first
@@ -145,17 +162,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int kb0 = sp * kper, kb1 = min(kblocks, (sp + 1) * kper);
       pre = min(C::kStages, kb1 - kb0);
       for (int j = 0; j < pre; ++j) {
+        const int kb = kb0 + j;
         uint8_t* st = smem + (size_t)j * C::kStageBytes;
         mbar_arrive_expect_tx(&full[j], C::kTxBytes);
         // bf16 W: the two 32-row halves of the SW128 tile; e4m3 W: the two
         // halves of the staging block after the tile (64 bytes per row).
         uint8_t* wdst = W8 ? st + kTcABytes + kTcWBytes : st + kTcABytes;
         const int half = W8 ? C::kW8Bytes / 2 : kTcWBytes / 2;
-        tma_load_2d(wdst, p.wmap, (kb0 + j) * kTcBK, r0, &full[j]);
-        tma_load_2d(wdst + half, p.wmap, (kb0 + j) * kTcBK, r1, &full[j]);
+        tma_load_2d(wdst, p.wmap, kb * kTcBK, r0, &full[j]);
+        tma_load_2d(wdst + half, p.wmap, kb * kTcBK, r1, &full[j]);
       }
     }
+    TC_STAMP(1);
     pdl_wait();
+    TC_STAMP(2);
     uint32_t s = 0, ph = 0;
     int issued = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
@@ -194,6 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc_wait(W8 ? &conv[s] : &full[s], ph, p, &abort_flag)) { ok = false; break; }
+        if (kb - kb0 < 24) TC_STAMP(4 + kb - kb0);
         tc_fence_after();
         const uint32_t a = smem_u32(smem + (size_t)s * C::kStageBytes);
         const uint32_t w = a + kTcABytes;
@@ -205,6 +226,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (!ok) break;
       tc_commit(&tfull[buf]);
+      TC_STAMP(30);
     }
   } else if (W8 && (warp == 2 || warp == 3)) {
     // ---- e4m3 -> bf16 converter (W8 only) ----
@@ -252,6 +274,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int buf = i & 1;
       // All four epilogue warps leave together (they share named barriers).
       if (bar_any(2, 128, !tc_wait(&tfull[buf], ((uint32_t)i >> 1) & 1u, p, &abort_flag))) break;
+      if (threadIdx.x == 128) TC_STAMP(31);
       tc_fence_after();
       float v[64];
       {
@@ -274,6 +297,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int c = 0; c < 64; ++c) tile[(row - 64) * kTcCombStride + c] = v[c];
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (threadIdx.x == 128) TC_STAMP(32);
       bool do_epi = true;
       if (q < 2) {
 #pragma unroll
@@ -293,6 +317,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           asm volatile("bar.sync 3, 64;" ::: "memory");
           do_epi = last_flag != 0;
+          if (threadIdx.x == 128) TC_STAMP(33);
           if (do_epi) {
             __threadfence();
 #pragma unroll
@@ -309,6 +334,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (threadIdx.x == 128) TC_STAMP(34);
       if (q < 2 && do_epi) {
         if constexpr (W8) {
           // W = scale * e4m3: column c of the tile is W row r0 + c (c < 32)
@@ -333,6 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) TC_STAMP(35);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTcTmemCols);
