@@ -107,3 +107,15 @@ def test_plan_covers_every_byte_once(name, pos):
     # Long contexts are capped at 8 split-KV chunks per head, which leaves
     # the CTAs holding attention items ~7% heavier at 8k positions.
     assert b.max() / b.mean() < (1.06 if pos <= 1024 else 1.10)
+
+
+def test_extension_argument_checks_without_a_device():
+    """Argument checks that return before any CUDA call."""
+    L = lib()
+    assert L.megakernel_set_merge_mode(None, 1) == -1
+    arr = (ctypes.c_longlong * 310)()
+    # unknown storage flags: refused before the weights are touched
+    assert L.megakernel_batch_init_ex(ctypes.c_void_p(16), arr, 310, 4, 64, 4) is None
+    assert L.megakernel_batch_init_ex(ctypes.c_void_p(16), arr, 310, 4, 64, -1) is None
+    assert L.megakernel_tp_exchange_slots(None, None) == -1
+    assert L.megakernel_tc_gemm_test_e4m3(None, 64, None, None, 1024, 1024, None, None) == -1

@@ -54,3 +54,20 @@ def test_greedy_sequence_is_oracle_greedy():
 def test_rope_tables_match_hf():
     c, s = rope_tables(64, 1e6, 8)
     assert torch.allclose(c[0], torch.ones(32)) and torch.allclose(s[0], torch.zeros(32))
+
+
+def test_e4m3_weight_rounding():
+    """quant_rows_e4m3 (the oracle's model of the batched decoder's e4m3
+    weights): each row's largest magnitude maps to 448 x its scale, every
+    value is an e4m3 number times the row scale, and the relative rounding
+    error stays within e4m3's 2^-4."""
+    from oracle.qwen3_decode import quant_rows_e4m3
+    g = torch.Generator().manual_seed(0)
+    w = (torch.randn(64, 256, generator=g) * 0.02).to(torch.bfloat16).float()
+    q = quant_rows_e4m3(w)
+    sc = w.abs().amax(dim=1, keepdim=True) / 448.0
+    assert torch.allclose(q.abs().amax(dim=1, keepdim=True), w.abs().amax(dim=1, keepdim=True), rtol=1e-6)
+    e = (q / sc)
+    assert torch.allclose(e.to(torch.float8_e4m3fn).float(), e, rtol=1e-5, atol=0)
+    big = w.abs() > 1e-2 * w.abs().amax(dim=1, keepdim=True)
+    assert ((q - w).abs()[big] / w.abs()[big]).max() <= 2.0 ** -4
