@@ -225,29 +225,34 @@ struct EpiResid {
     const __nv_bfloat16* g;
   };
   __device__ __forceinline__ static void apply(const Params&, int, int, float (&)[64]) {}
-  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int c) {
+  // 128 threads: column c = tid & 63 for rows 32 (tid >> 6) .. +31, then
+  // the per-row sum of squares on 64 threads.
+  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid) {
     const BatchDev& d = ep.d;
+    const int c = tid & 63, r0 = 32 * (tid >> 6);
     const int col = 64 * t + c;
     const float g = __bfloat162float(ep.g[col]);
-    float xv[kBMax];   // all loads in flight before the first use
+    float xv[kBMax / 2];   // all loads in flight before the first use
 #pragma unroll
-    for (int r = 0; r < kBMax; ++r) xv[r] = __ldcg(d.x + (size_t)r * kBH + col);
+    for (int r = 0; r < kBMax / 2; ++r) xv[r] = __ldcg(d.x + (size_t)(r0 + r) * kBH + col);
 #pragma unroll
-    for (int r = 0; r < kBMax; ++r) {
-      const float xn = xv[r] + tile[r * kTcCombStride + c];
-      __stcg(d.x + (size_t)r * kBH + col, xn);
-      tile[r * kTcCombStride + c] = xn;
-      put_hilo(ep.a_next, kBH, r, col, g * xn);
+    for (int r = 0; r < kBMax / 2; ++r) {
+      const float xn = xv[r] + tile[(r0 + r) * kTcCombStride + c];
+      __stcg(d.x + (size_t)(r0 + r) * kBH + col, xn);
+      tile[(r0 + r) * kTcCombStride + c] = xn;
+      put_hilo(ep.a_next, kBH, r0 + r, col, g * xn);
     }
-    asm volatile("bar.sync 3, 64;" ::: "memory");
-    const int row = c;
-    float ss = 0.f;
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+    if (tid < 64) {
+      const int row = tid;
+      float ss = 0.f;
 #pragma unroll 8
-    for (int k = 0; k < 64; ++k) {
-      const float xv = tile[row * kTcCombStride + k];
-      ss = fmaf(xv, xv, ss);
+      for (int k = 0; k < 64; ++k) {
+        const float xv = tile[row * kTcCombStride + k];
+        ss = fmaf(xv, xv, ss);
+      }
+      d.ssq[t * kBMax + row] = ss;
     }
-    d.ssq[t * kBMax + row] = ss;
   }
 };
 
@@ -271,7 +276,7 @@ struct EpiSwiGLU {
   __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid) {
     const int c = tid & 31;
 #pragma unroll 4
-    for (int r = tid >> 5; r < kBMax; r += 2) put_hilo(ep.d.a_h, kBI, r, 32 * t + c, tile[r * kTcCombStride + c]);
+    for (int r = tid >> 5; r < kBMax; r += 4) put_hilo(ep.d.a_h, kBI, r, 32 * t + c, tile[r * kTcCombStride + c]);
   }
 };
 

@@ -16,9 +16,10 @@
 //               per row), release the accumulator, add hi + lo through shared
 //               memory, (split K) publish / collect the parts, then
 //               Epi::apply(ep, tile, seq, v[64]) on 64 threads (one per row)
-//               and, when Epi::kCols, Epi::cols(ep, tile, smem_tile, c) with
-//               the 64 x 64 tile in shared memory and one thread per column,
-//               so global writes are coalesced.
+//               and, when Epi::kCols, Epi::cols(ep, tile, smem_tile, tid) on
+//               all 128 epilogue threads with the 64 x 64 tile in shared
+//               memory (lanes = consecutive columns, so global writes are
+//               coalesced).
 // Every wait is bounded (timeout_ns); on expiry the kernel records
 // MK_ERR_TIMEOUT in *err and every role leaves its loop.
 #pragma once
@@ -316,21 +317,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (old == p.ksplit - 1) p.counters[t] = 0;
           }
           asm volatile("bar.sync 3, 64;" ::: "memory");
-          do_epi = last_flag != 0;
           if (threadIdx.x == 128) TC_STAMP(33);
-          if (do_epi) {
-            __threadfence();
+        }
+      }
+      if (p.ksplit > 1) {
+        // The last part's CTA sums all parts in split order (deterministic)
+        // with all 128 epilogue threads, each half a row, every load of all
+        // parts in flight at once (one L2 round trip per 4 parts), and hands
+        // the rows to their owners through shared memory.
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        do_epi = last_flag != 0;
+        if (do_epi) {
+          __threadfence();
+          const int rr = 32 * (q & 1) + lane, c0 = 32 * (q >> 1);
+          float acc[32];
 #pragma unroll
-            for (int c = 0; c < 64; ++c) v[c] = 0.f;
-            for (int k = 0; k < p.ksplit; ++k) {
-              const float* pr = p.ws + (((size_t)t * p.ksplit + k) * 64 + row) * 64;
+          for (int c = 0; c < 32; ++c) acc[c] = 0.f;
+          for (int k0 = 0; k0 < p.ksplit; k0 += 4) {
+            float4 a[4][8];
 #pragma unroll
-              for (int c = 0; c < 64; c += 4) {
-                const float4 a = __ldcg(reinterpret_cast<const float4*>(pr + c));
-                v[c] += a.x; v[c + 1] += a.y; v[c + 2] += a.z; v[c + 3] += a.w;
+            for (int kk = 0; kk < 4; ++kk)
+              if (k0 + kk < p.ksplit) {
+                const float* pr = p.ws + (((size_t)t * p.ksplit + k0 + kk) * 64 + rr) * 64 + c0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a[kk][j] = __ldcg(reinterpret_cast<const float4*>(pr) + j);
               }
-            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              if (k0 + kk < p.ksplit) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  acc[4 * j] += a[kk][j].x; acc[4 * j + 1] += a[kk][j].y;
+                  acc[4 * j + 2] += a[kk][j].z; acc[4 * j + 3] += a[kk][j].w;
+                }
+              }
           }
+#pragma unroll
+          for (int c = 0; c < 32; ++c) tile[rr * kTcCombStride + c0 + c] = acc[c];
+          if (threadIdx.x == 128) TC_STAMP(36);
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (q < 2 && do_epi) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) v[c] = tile[row * kTcCombStride + c];
         }
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
@@ -345,14 +374,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int c = 0; c < 64; ++c) v[c] *= __ldg(p.wscale + (c < 32 ? r0 + c : r1 + c - 32));
         }
         Epi::apply(ep, t, row, v);
+        if (threadIdx.x == 128) TC_STAMP(37);
         // Column phase: the row values go through shared memory so that
         // global writes are coalesced (lanes = consecutive columns).
         if constexpr (Epi::kCols) {
 #pragma unroll
           for (int c = 0; c < 64; ++c) tile[row * kTcCombStride + c] = v[c];
-          asm volatile("bar.sync 3, 64;" ::: "memory");
-          Epi::cols(ep, t, tile, row);
         }
+      }
+      if constexpr (Epi::kCols) {
+        // do_epi is the same for all 128 epilogue threads.
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (do_epi) Epi::cols(ep, t, tile, threadIdx.x - 128);
+        if (threadIdx.x == 128) TC_STAMP(38);
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
     }
