@@ -169,6 +169,13 @@ int megakernel_decode_noalloc(const void* d_weights, const long long* offsets, i
  * Returns MK_OK or an MK_ERR_* code. */
 int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d_w, int K, int N, float* d_out,
                             void* stream);
+/* The same with K split over `ksplit` (1..4) CTAs per 64-column output tile:
+ * the CTAs of a tile form a thread-block cluster, ranks 1..ksplit-1 push
+ * their partial tiles into rank 0's shared memory and rank 0 sums them (the
+ * split-K path of the batched O and down projections).  Every split must keep at least one
+ * 64-column K block (MK_ERR_INVALID_ARG otherwise). */
+int megakernel_tc_gemm_test_split(const float* d_x, int rows, const void* d_w, int K, int N, int ksplit,
+                                  float* d_out, void* stream);
 /* The same on e4m3 weights: d_w8 [N][K] e4m3 bytes with per-row scales
  * d_scale[N] (W = scale * e4m3), through the GEMM's e4m3 -> bf16 converter
  * warps (the path megakernel_batch_init_ex(..., MK_W_FP8_E4M3) runs). */

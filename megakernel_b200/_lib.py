@@ -109,6 +109,7 @@ def signatures() -> dict:
         "megakernel_decode_noalloc": ([vp, llp, c_int, vp, c_int, c_int, vp, c_int, c_int, vp, vp, vp],
                                       c_int),
         "megakernel_tc_gemm_test": ([vp, c_int, vp, c_int, c_int, vp, vp], c_int),
+        "megakernel_tc_gemm_test_split": ([vp, c_int, vp, c_int, c_int, c_int, vp, vp], c_int),
         "megakernel_tc_gemm_test_e4m3": ([vp, c_int, vp, vp, c_int, c_int, vp, vp], c_int),
         "megakernel_prefill": ([vp, vp, c_int, vp, vp], c_int),
         "megakernel_batch_init": ([vp, llp, c_int, c_int, c_int], vp),

@@ -31,12 +31,14 @@ __global__ void hilo_split_kernel(const float* __restrict__ x, int rows, int K, 
 // Plain epilogue: out[seq][64 t + c] = v[c] for seq < rows.
 struct EpiStore {
   static constexpr bool kCols = false;
+  static constexpr int kPre = 0;
   struct Params {
     float* out;
     int ldo;
     int rows;
   };
-  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, const float (&v)[64]) {
+  __device__ __forceinline__ static void prefetch(const Params&, int, float*, int) {}
+  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, const float (&v)[64], const float*) {
     if (seq >= ep.rows) return;
     float* o = ep.out + (size_t)seq * ep.ldo + 64 * t;
 #pragma unroll
@@ -74,8 +76,6 @@ struct BatchDev {
   int* pos;              // [64] position of each sequence's next token
   int* err;
   int* acnt;             // [64][8] attention chunk tickets (0 between layers)
-  float* ws;             // split-K partials (2 MB)
-  int* tickets;          // split-K arrival counters [64]
   int batch, max_seq, maxch;
   int seq_mode;          // 0: row b is sequence b; 1: every row belongs to sequence 0 (prefill)
 };
@@ -102,6 +102,11 @@ __device__ __forceinline__ float inv_rms(const float* ssq, int seq) {
 #pragma unroll
   for (int t = 0; t < kBHT; ++t) s += ssq[t * kBMax + seq];
   return rsqrtf(s / (float)kBH + 1e-6f);
+}
+// Epilogue prefetch (128 threads, e = 0..127): 1 / rms of every row into
+// pre[0..63].
+__device__ __forceinline__ void prefetch_inv_rms(const float* ssq, float* pre, int e) {
+  if (e < kBMax) pre[e] = inv_rms(ssq, e);
 }
 __device__ __forceinline__ void put_hilo(__nv_bfloat16* a, int K, int seq, int col, float v) {
   const __nv_bfloat16 hi = __float2bfloat16_rn(v);
@@ -149,29 +154,50 @@ __global__ void bembed_kernel(BatchDev d, const __nv_bfloat16* __restrict__ emb,
 // sequence's position, writes q (fp32) or appends K / V (bf16) to the cache.
 struct EpiQKV {
   static constexpr bool kCols = false;
+  // pre: [0, 64) 1/rms per row, [64, 128) head-norm gains, [128, 192) the
+  // row's position (int bits), then [192 + 64 r, +64) cos | sin of row r.
+  static constexpr int kPre = 3 * 64 + 64 * 64;
   struct Params {
     BatchDev d;
     int l;
     const __nv_bfloat16* qn;
     const __nv_bfloat16* kn;
   };
-  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, float (&v)[64]) {
+  __device__ __forceinline__ static void prefetch(const Params& ep, int t, float* pre, int e) {
+    const BatchDev& d = ep.d;
+    prefetch_inv_rms(d.ssq, pre, e);
+    if (e < 64) {
+      pre[64 + e] = t < 24 ? __bfloat162float((t < 16 ? ep.qn : ep.kn)[e]) : 0.f;
+      pre[128 + e] = __int_as_float(e < d.batch ? __ldcg(d.pos + e) : 0);
+    }
+    if (t < 24) {
+      // cos | sin rows of each sequence's position: thread e covers 32
+      // consecutive floats of row e / 2 (lanes = consecutive addresses).
+      const int r = e >> 1, half = e & 1;
+      const int pr = r < d.batch ? __ldcg(d.pos + r) : 0;
+      const float* src = (half ? d.rope_sin : d.rope_cos) + (size_t)pr * 32;
+      float* dst = pre + 192 + 64 * r + 32 * half;
+#pragma unroll
+      for (int c = 0; c < 32; c += 4) *reinterpret_cast<float4*>(dst + c) = __ldg(reinterpret_cast<const float4*>(src + c));
+    }
+  }
+  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, float (&v)[64], const float* pre) {
     const BatchDev& d = ep.d;
     if (seq >= d.batch) return;
-    const float r = inv_rms(d.ssq, seq);
+    const float r = pre[seq];
 #pragma unroll
     for (int c = 0; c < 64; ++c) v[c] *= r;
-    const int p = d.pos[seq];
+    const int p = __float_as_int(pre[128 + seq]);
     if (t < 24) {
-      const __nv_bfloat16* gn = t < 16 ? ep.qn : ep.kn;
+      const float* gn = pre + 64;
       float ss = 0.f;
 #pragma unroll
       for (int c = 0; c < 64; ++c) ss = fmaf(v[c], v[c], ss);
       const float rr = rsqrtf(ss / 64.f + 1e-6f);
 #pragma unroll
-      for (int c = 0; c < 64; ++c) v[c] = __bfloat162float(gn[c]) * (v[c] * rr);
-      const float* cs = d.rope_cos + (size_t)p * 32;
-      const float* sn = d.rope_sin + (size_t)p * 32;
+      for (int c = 0; c < 64; ++c) v[c] = gn[c] * (v[c] * rr);
+      const float* cs = pre + 192 + 64 * seq;
+      const float* sn = cs + 32;
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
         const float x0 = v[c], x1 = v[c + 32], cc = cs[c], ssn = sn[c];
@@ -219,25 +245,36 @@ struct EpiQKV {
 // then thread = column again: hi/lo of (g . x) into a_next.
 struct EpiResid {
   static constexpr bool kCols = true;
+  // pre: [0, 64) gains of the tile's columns, then x[r][64 t + c] at
+  // 64 + 64 r + c (the residual stream's tile, fetched during the MMAs).
+  static constexpr int kPre = 64 + 64 * 64;
   struct Params {
     BatchDev d;
     __nv_bfloat16* a_next;
     const __nv_bfloat16* g;
   };
-  __device__ __forceinline__ static void apply(const Params&, int, int, float (&)[64]) {}
+  __device__ __forceinline__ static void prefetch(const Params& ep, int t, float* pre, int e) {
+    const BatchDev& d = ep.d;
+    if (e < 64) pre[e] = __bfloat162float(ep.g[64 * t + e]);
+    // Row r = e / 2, 32 columns per thread, 16-byte loads through L2 (the
+    // previous kernel wrote x).
+    const int r = e >> 1, c0 = 32 * (e & 1);
+    const float* src = d.x + (size_t)r * kBH + 64 * t + c0;
+    float* dst = pre + 64 + 64 * r + c0;
+#pragma unroll
+    for (int c = 0; c < 32; c += 4) *reinterpret_cast<float4*>(dst + c) = __ldcg(reinterpret_cast<const float4*>(src + c));
+  }
+  __device__ __forceinline__ static void apply(const Params&, int, int, float (&)[64], const float*) {}
   // 128 threads: column c = tid & 63 for rows 32 (tid >> 6) .. +31, then
   // the per-row sum of squares on 64 threads.
-  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid) {
+  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid, const float* pre) {
     const BatchDev& d = ep.d;
     const int c = tid & 63, r0 = 32 * (tid >> 6);
     const int col = 64 * t + c;
-    const float g = __bfloat162float(ep.g[col]);
-    float xv[kBMax / 2];   // all loads in flight before the first use
-#pragma unroll
-    for (int r = 0; r < kBMax / 2; ++r) xv[r] = __ldcg(d.x + (size_t)(r0 + r) * kBH + col);
+    const float g = pre[c];
 #pragma unroll
     for (int r = 0; r < kBMax / 2; ++r) {
-      const float xn = xv[r] + tile[(r0 + r) * kTcCombStride + c];
+      const float xn = pre[64 + 64 * (r0 + r) + c] + tile[(r0 + r) * kTcCombStride + c];
       __stcg(d.x + (size_t)(r0 + r) * kBH + col, xn);
       tile[(r0 + r) * kTcCombStride + c] = xn;
       put_hilo(ep.a_next, kBH, r0 + r, col, g * xn);
@@ -246,10 +283,14 @@ struct EpiResid {
     if (tid < 64) {
       const int row = tid;
       float ss = 0.f;
-#pragma unroll 8
-      for (int k = 0; k < 64; ++k) {
-        const float xv = tile[row * kTcCombStride + k];
-        ss = fmaf(xv, xv, ss);
+      const float4* tr = reinterpret_cast<const float4*>(tile + row * kTcCombStride);
+#pragma unroll 4
+      for (int k = 0; k < 16; ++k) {
+        const float4 xv = tr[k];
+        ss = fmaf(xv.x, xv.x, ss);
+        ss = fmaf(xv.y, xv.y, ss);
+        ss = fmaf(xv.z, xv.z, ss);
+        ss = fmaf(xv.w, xv.w, ss);
       }
       d.ssq[t * kBMax + row] = ss;
     }
@@ -257,26 +298,28 @@ struct EpiResid {
 };
 
 // Gate/up epilogue: columns 0..31 are gate rows 32t.., 32..63 the matching
-// up rows.  Row phase: h = silu(gate / rms) * (up / rms) into v[0..31];
-// column phase: hi/lo of h into a_h (coalesced).
+// up rows.  Column phase on all 128 epilogue threads (lane = gate column c,
+// so the hi/lo writes to a_h are coalesced): h = silu(gate / rms) *
+// (up / rms), then hi/lo of h into a_h.
 struct EpiSwiGLU {
   static constexpr bool kCols = true;
+  static constexpr int kPre = 64;   // 1 / rms per row
   struct Params {
     BatchDev d;
   };
-  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, float (&v)[64]) {
-    const BatchDev& d = ep.d;
-    const float r = inv_rms(d.ssq, seq);
-#pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      const float gt = v[c] * r, up = v[32 + c] * r;
-      v[c] = seq < d.batch ? gt / (1.f + expf(-gt)) * up : 0.f;
-    }
+  __device__ __forceinline__ static void prefetch(const Params& ep, int, float* pre, int e) {
+    prefetch_inv_rms(ep.d.ssq, pre, e);
   }
-  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid) {
+  __device__ __forceinline__ static void apply(const Params&, int, int, float (&)[64], const float*) {}
+  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid, const float* pre) {
     const int c = tid & 31;
+    const int batch = ep.d.batch;
 #pragma unroll 4
-    for (int r = tid >> 5; r < kBMax; r += 4) put_hilo(ep.d.a_h, kBI, r, 32 * t + c, tile[r * kTcCombStride + c]);
+    for (int r = tid >> 5; r < kBMax; r += 4) {
+      const float rr = pre[r];
+      const float gt = tile[r * kTcCombStride + c] * rr, up = tile[r * kTcCombStride + 32 + c] * rr;
+      put_hilo(ep.d.a_h, kBI, r, 32 * t + c, r < batch ? gt / (1.f + expf(-gt)) * up : 0.f);
+    }
   }
 };
 
@@ -284,14 +327,18 @@ struct EpiSwiGLU {
 // (value, lowest index) of the tile -> lm_part[t][seq]; optional logits.
 struct EpiArgmax {
   static constexpr bool kCols = false;
+  static constexpr int kPre = 64;   // 1 / rms per row
   struct Params {
     BatchDev d;
     float* logits;  // [batch][V] or null
   };
-  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, float (&v)[64]) {
+  __device__ __forceinline__ static void prefetch(const Params& ep, int, float* pre, int e) {
+    prefetch_inv_rms(ep.d.ssq, pre, e);
+  }
+  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, float (&v)[64], const float* pre) {
     const BatchDev& d = ep.d;
     if (seq >= d.batch) return;
-    const float r = inv_rms(d.ssq, seq);
+    const float r = pre[seq];
     float best = -INFINITY;
     int bi = 0;
 #pragma unroll
@@ -733,9 +780,10 @@ __global__ void bargmax_kernel(BatchDev d, int* __restrict__ out) {
 }  // namespace mk
 
 // Test entry point (see include/megakernel.h).
-extern "C" int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d_w, int K, int N, float* d_out,
-                                       void* stream) {
-  if (!d_x || !d_w || !d_out || rows < 1 || rows > 64 || K < 64 || K % 64 != 0 || N < 64 || N % 64 != 0)
+extern "C" int megakernel_tc_gemm_test_split(const float* d_x, int rows, const void* d_w, int K, int N, int ksplit,
+                                             float* d_out, void* stream) {
+  if (!d_x || !d_w || !d_out || rows < 1 || rows > 64 || K < 64 || K % 64 != 0 || N < 64 || N % 64 != 0 ||
+      ksplit < 1 || ksplit > mk::kTcMaxSplit || (ksplit - 1) * ((K / 64 + ksplit - 1) / ksplit) >= K / 64)
     return MK_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int dev = 0, sms = 0;
@@ -756,7 +804,7 @@ extern "C" int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d
       cudaMemcpyAsync(maps, h, sizeof(h), cudaMemcpyHostToDevice, st);
       cudaMemsetAsync(err, 0, sizeof(int), st);
       mk::hilo_split_kernel<<<64, 256, 0, st>>>(d_x, rows, K, a);
-      mk::TcGemmParams p{maps, maps + 1, K, N / 64, 0, err, 1000000000LL, 1, nullptr, nullptr};
+      mk::TcGemmParams p{maps, maps + 1, K, N / 64, 0, err, 1000000000LL, ksplit, nullptr};
       mk::EpiStore::Params ep{d_out, N, rows};
       if (mk::tc_gemm_launch<mk::EpiStore>(p, ep, sms, st) != cudaSuccess) rc = MK_ERR_LAUNCH;
       int herr = 0;
@@ -771,6 +819,11 @@ extern "C" int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d
   cudaFree(maps);
   cudaFree(err);
   return rc;
+}
+
+extern "C" int megakernel_tc_gemm_test(const float* d_x, int rows, const void* d_w, int K, int N, float* d_out,
+                                       void* stream) {
+  return megakernel_tc_gemm_test_split(d_x, rows, d_w, K, N, 1, d_out, stream);
 }
 
 // The same GEMM on e4m3 weights: d_w8 [N][K] e4m3 bytes, d_scale [N] per-row
@@ -800,7 +853,7 @@ extern "C" int megakernel_tc_gemm_test_e4m3(const float* d_x, int rows, const vo
       cudaMemcpyAsync(maps, h, sizeof(h), cudaMemcpyHostToDevice, st);
       cudaMemsetAsync(err, 0, sizeof(int), st);
       mk::hilo_split_kernel<<<64, 256, 0, st>>>(d_x, rows, K, a);
-      mk::TcGemmParams p{maps, maps + 1, K, N / 64, 0, err, 1000000000LL, 1, nullptr, nullptr, d_scale};
+      mk::TcGemmParams p{maps, maps + 1, K, N / 64, 0, err, 1000000000LL, 1, d_scale};
       mk::EpiStore::Params ep{d_out, N, rows};
       if (mk::tc_gemm_launch<mk::EpiStore, true>(p, ep, sms, st) != cudaSuccess) rc = MK_ERR_LAUNCH;
       int herr = 0;
@@ -872,17 +925,14 @@ __global__ void quant_rows_kernel(const __nv_bfloat16* __restrict__ w, int rows,
 }
 
 enum { kMapAx = 0, kMapAatt = 1, kMapAh = 2, kMapLayer0 = 3 };
-constexpr size_t kBWsBytes = (size_t)2 << 20;
-
-// GEMM launch parameters with K split over `ksplit` CTAs per output tile
-// (every split keeps at least one K block; partials fit the workspace).
+// GEMM launch parameters with K split over `ksplit` CTAs (one cluster) per
+// output tile; every split keeps at least one K block.
 mk::TcGemmParams gemm_params(const mk::BatchDev& d, const CUtensorMap* a, const CUtensorMap* w, int K, int ntiles,
                              int half_off, int ksplit) {
   const int kb = K / mk::kTcBK;
-  while (ksplit > 1 && ((ksplit - 1) * ((kb + ksplit - 1) / ksplit) >= kb ||
-                        (size_t)ntiles * ksplit * 64 * 64 * 4 > kBWsBytes || ntiles > 64))
-    --ksplit;
-  return mk::TcGemmParams{a, w, K, ntiles, half_off, d.err, 1000000000LL, ksplit, d.ws, d.tickets};
+  if (ksplit > mk::kTcMaxSplit) ksplit = mk::kTcMaxSplit;
+  while (ksplit > 1 && (ksplit - 1) * ((kb + ksplit - 1) / ksplit) >= kb) --ksplit;
+  return mk::TcGemmParams{a, w, K, ntiles, half_off, d.err, 1000000000LL, ksplit, nullptr};
 }
 inline int map_layer(int l, int k) { return kMapLayer0 + 4 * l + k; }   // k: 0 qkv, 1 o, 2 gate/up, 3 down
 inline int map_lm() { return kMapLayer0 + 4 * mk::kBL; }
@@ -896,7 +946,7 @@ void batch_free(BatchState* s) {
   cudaFree(s->wsc);
   cudaFree(s->d_tmp);
   cudaFree(const_cast<float*>(s->d.rope_cos)); cudaFree(const_cast<float*>(s->d.rope_sin));
-  cudaFree(s->d.pos); cudaFree(s->d.err); cudaFree(s->maps); cudaFree(s->d.ws); cudaFree(s->d.tickets); cudaFree(s->d.acnt);
+  cudaFree(s->d.pos); cudaFree(s->d.err); cudaFree(s->maps); cudaFree(s->d.acnt);
   delete s;
 }
 
@@ -951,7 +1001,6 @@ BatchState* batch_init(const void* d_weights, const long long* offsets, int num_
       balloc(&s->d_tmp, sizeof(int) * kBMax) && balloc(&rc, sizeof(float) * (size_t)max_seq * 32) &&
       balloc(&rs, sizeof(float) * (size_t)max_seq * 32) && balloc(&d.pos, sizeof(int) * kBMax) &&
       balloc(&d.err, sizeof(int) * 4) && balloc(&s->maps, sizeof(CUtensorMap) * (map_lm() + 1)) &&
-      balloc(&d.ws, kBWsBytes) && balloc(&d.tickets, sizeof(int) * 64) &&
       balloc(&d.acnt, sizeof(int) * kBMax * kBNKV);
   d.rope_cos = rc;
   d.rope_sin = rs;
@@ -1054,17 +1103,37 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
     attn_attr = true;
   }
   const bool f8 = d.kv8 != nullptr;
-  // Split-K factors of the q/k/v, O, gate/up and down GEMMs.  Measured on
-  // B200 (64 sequences at position 1024, ms per step): {4, 8, 1, 8} 3.21,
-  // {2, 4, 1, 4} 2.83, {1, 1, 1, 1} 2.92, {1, 2, 1, 3} 2.72 -- the split-K
-  // fixup (partials through L2, a ticket, the last CTA summing them) costs
-  // more than the extra CTAs save.
-  constexpr int ks[4] = {1, 2, 1, 3};
+  // Split-K factors of the q/k/v, O, gate/up and down GEMMs (cluster
+  // split K, partials pushed into rank 0's shared memory).  Measured on B200
+  // (64 sequences at position 1024, ms per step): {1, 2, 1, 3} 2.049,
+  // {1, 2, 1, 4} 2.030, {1, 1, 1, 4} 2.095, {2, 2, 1, 4} 2.033,
+  // {1, 2, 2, 4} 2.178, {2, 2, 2, 4} 2.164.  (The earlier form -- partials
+  // through global memory, a ticket, the last CTA summing, epilogue inputs
+  // loaded after the MMAs -- took 2.463 at {1, 2, 1, 3}.)
+  int ks[4] = {1, 2, 1, 4};
+  if (const char* e = getenv("MK_BATCH_KSPLIT")) {
+    int t[4];
+    if (sscanf(e, "%d,%d,%d,%d", &t[0], &t[1], &t[2], &t[3]) == 4)
+      for (int k = 0; k < 4; ++k) ks[k] = t[k] < 1 ? 1 : (t[k] > kTcMaxSplit ? kTcMaxSplit : t[k]);
+  }
   const bool w8 = s->w8 != nullptr;
   // GEMM of map slot m (layer l, kind k; m = 4L: LM head) on the bf16 or
   // the e4m3 weights.
+#if MK_TC_STAMPS
+  int tl_next = 0;
+  {
+    void* tl = nullptr;
+    if (cudaGetSymbolAddress(&tl, g_tc_tl) == cudaSuccess) cudaMemsetAsync(tl, 0xff, sizeof(g_tc_tl), st);
+    if (cudaGetSymbolAddress(&tl, g_tc_stamps) == cudaSuccess) cudaMemsetAsync(tl, 0, sizeof(g_tc_stamps), st);
+  }
+#endif
   auto gemm = [&](auto epi_tag, TcGemmParams p, const auto& ep, int m) -> cudaError_t {
     using Epi = typename decltype(epi_tag)::type;
+#if MK_TC_STAMPS
+    p.tl = tl_next++;
+    const char* ss = getenv("MK_TC_STAMP_SLOT");
+    p.stamp = ss != nullptr && atoi(ss) == p.tl;
+#endif
     if (!w8) return tc_gemm_launch<Epi, false>(p, ep, s->sms, st);
     p.wscale = s->wsc + s->sc_off[m];
     return tc_gemm_launch<Epi, true>(p, ep, s->sms, st);
@@ -1167,6 +1236,11 @@ extern "C" int megakernel_prefill(void* handle, const int* d_tokens, int n_token
 // Profiling build only: copies the GEMM stamps [256][64] (u64 ns) to host.
 extern "C" int megakernel_tc_stamps(void* h_out) {
   return cudaMemcpyFromSymbol(h_out, mk::g_tc_stamps, sizeof(mk::g_tc_stamps)) == cudaSuccess ? 0 : -2;
+}
+// Profiling build only: the last step's GEMM timeline [160][3] (u64 ns:
+// first entry, first release from griddepcontrol.wait, ~last exit).
+extern "C" int megakernel_tc_timeline(void* h_out) {
+  return cudaMemcpyFromSymbol(h_out, mk::g_tc_tl, sizeof(mk::g_tc_tl)) == cudaSuccess ? 0 : -2;
 }
 #endif
 

@@ -20,6 +20,14 @@
 //               all 128 epilogue threads with the 64 x 64 tile in shared
 //               memory (lanes = consecutive columns, so global writes are
 //               coalesced).
+// Split K (ksplit = S, 2..4): the S CTAs of one output tile form a
+// thread-block cluster (cluster rank = split index).  Ranks 1..S-1 push
+// their hi + lo partial tiles into rank 0's receive buffers with st.async
+// (distributed shared memory, completing on rank 0's "recv" mbarrier by
+// byte count, so no release fence is needed); rank 0 adds them to its own
+// partial in rank order (deterministic), frees the buffers with a remote
+// arrive on each peer's "free" mbarrier and runs the epilogue.  No partial
+// crosses L2 and no counter is needed.
 // Every wait is bounded (timeout_ns); on expiry the kernel records
 // MK_ERR_TIMEOUT in *err and every role leaves its loop.
 #pragma once
@@ -34,23 +42,34 @@
 
 namespace mk {
 
-constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 8;
+constexpr int kTcBM = 128, kTcBN = 64, kTcBK = 64, kTcStages = 5;
 constexpr int kTcABytes = kTcBM * kTcBK * 2;          // 16 KB
 constexpr int kTcWBytes = kTcBN * kTcBK * 2;          //  8 KB
 constexpr int kTcStageBytes = kTcABytes + kTcWBytes;  // 24 KB
 constexpr int kTcThreads = 256;
-constexpr int kTcCombStride = 65;                     // floats per row of the hi/lo combine buffer
-constexpr size_t kTcSmemBytes = 1024 + (size_t)kTcStages * kTcStageBytes + 64 * kTcCombStride * 4;
-// Per-instance ring: with e4m3 weights (W8) each stage also holds the 4 KB
-// e4m3 W block that two converter warps expand into the bf16 W tile, and the
-// ring has 7 stages (shared memory).
+// Floats per row of the 64 x 64 tile buffer (hi/lo combine, split-K
+// partial, epilogue tile): 68 keeps rows 16-byte aligned, and row-wise float4
+// accesses of 8 consecutive rows (one quarter warp) hit 32 distinct banks.
+constexpr int kTcCombStride = 68;
+// Epilogue side inputs fetched while the MMAs run (kTcPreFloats floats):
+// [0, 64) the tile's per-column W scales (e4m3 weights), then the Epi's own
+// region of Epi::kPre floats (at most kTcPreFloats - 64).
+constexpr int kTcPreFloats = 64 + 64 * 64 + 3 * 64;
+// Split K: at most 4 CTAs per tile, so rank 0 receives up to 3 partial tiles.
+constexpr int kTcMaxSplit = 4;
+constexpr int kTcRecvFloats = (kTcMaxSplit - 1) * 64 * kTcCombStride;
+// Per-instance ring: 5 stages of A + W (measured on B200: 4 to 8 stages give
+// the same step time); with e4m3 weights (W8) each stage also holds the 4 KB
+// e4m3 W block that two converter warps expand into the bf16 W tile.
 template <bool W8>
 struct TcCfg {
-  static constexpr int kStages = W8 ? 7 : kTcStages;
+  static constexpr int kStages = kTcStages;
   static constexpr int kW8Bytes = W8 ? kTcBN * kTcBK : 0;
   static constexpr int kStageBytes = kTcStageBytes + kW8Bytes;
   static constexpr uint32_t kTxBytes = W8 ? kTcABytes + kW8Bytes : kTcStageBytes;
-  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 64 * kTcCombStride * 4;
+  static constexpr size_t kSmem =
+      1024 + (size_t)kStages * kStageBytes + 64 * kTcCombStride * 4 + (size_t)kTcPreFloats * 4 +
+      (size_t)kTcRecvFloats * 4;
 };
 constexpr uint32_t kTcTmemCols = 128;                 // two 64-column accumulators
 
@@ -62,10 +81,10 @@ struct TcGemmParams {
   int w_half_off;           // gate/up: row offset of the second matrix; 0: plain rows
   int* err;
   long long timeout_ns;
-  int ksplit;               // K blocks split over this many CTAs per tile (1: no split)
-  float* ws;                // split partials [ntiles][ksplit][64][64] (ksplit > 1)
-  int* counters;            // [ntiles] arrival tickets, 0 between launches (ksplit > 1)
+  int ksplit;               // K blocks split over this many CTAs (one cluster) per tile, 1..4
   const float* wscale;      // e4m3 weights only: per-W-row scale (the GEMM uses W = scale * e4m3)
+  int tl = -1;              // profiling builds: this launch's slot in the step timeline
+  int stamp = 0;            // profiling builds: record this launch's per-CTA stamps
 };
 
 // W rows of tile t: [r0, r0+32) then [r1, r1+32).  Plain: 64t and 64t+32;
@@ -94,9 +113,27 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const Tc
   }
 }
 
-// Profiling build only (-DMK_TC_STAMPS=1): %globaltimer stamps of the
-// down-projection launches (K = 2816) per CTA, read back with
-// megakernel_tc_stamps; the last such launch of a step remains.
+// Same, acquire at cluster scope (the arrivals come from other CTAs).
+__device__ __forceinline__ bool tc_wait_cl(uint64_t* bar, uint32_t parity, const TcGemmParams& p,
+                                           volatile int* abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort_flag) return false;
+      if ((long long)(globaltimer_ns() - t0) > p.timeout_ns) {
+        atomicCAS(p.err, 0, MK_ERR_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Profiling build only (-DMK_TC_STAMPS=1): %globaltimer stamps per CTA of
+// the launch whose params carry `stamp` (batch_step marks the launch slot
+// named by MK_TC_STAMP_SLOT), read back with megakernel_tc_stamps.
 #ifndef MK_TC_STAMPS
 #define MK_TC_STAMPS 0
 #endif
@@ -104,10 +141,21 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const Tc
 __device__ unsigned long long g_tc_stamps[256][64];
 #define TC_STAMP(k)                                                                  \
   do {                                                                              \
-    if (p.K == 2816 && blockIdx.x < 256) g_tc_stamps[blockIdx.x][(k)] = globaltimer_ns(); \
+    if (p.stamp && blockIdx.x < 256) g_tc_stamps[blockIdx.x][(k)] = globaltimer_ns(); \
+  } while (0)
+// Step timeline: per GEMM launch of a step (slot p.tl), the earliest CTA
+// entry, the earliest release from griddepcontrol.wait and the latest CTA
+// exit (stored complemented so that all three are atomicMin), read back
+// with megakernel_tc_timeline.
+constexpr int kTcTimeline = 160;
+__device__ unsigned long long g_tc_tl[kTcTimeline][3];
+#define TC_TL(k, v)                                                      \
+  do {                                                                   \
+    if (p.tl >= 0 && p.tl < kTcTimeline) atomicMin(&g_tc_tl[p.tl][(k)], (v)); \
   } while (0)
 #else
 #define TC_STAMP(k) do {} while (0)
+#define TC_TL(k, v) do {} while (0)
 #endif
 
 // e4m3 pair (low byte first) -> bf16 pair, exactly (through f16).
@@ -127,7 +175,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
   float* comb = reinterpret_cast<float*>(smem + (size_t)C::kStages * C::kStageBytes);
+  float* pre = comb + 64 * kTcCombStride;
+  float* recv = pre + kTcPreFloats;        // split K, rank 0: partials of ranks 1..S-1 [S-1][64][kTcCombStride]
+  static_assert(Epi::kPre <= kTcPreFloats - 64, "epilogue prefetch region");
   __shared__ alignas(8) uint64_t full[kTcStages], empty[kTcStages], conv[kTcStages], tfull[2], tempty[2];
+  __shared__ alignas(8) uint64_t recv_bar, free_bar;   // split K (cluster) only
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
 
@@ -135,6 +187,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); mbar_init(&conv[s], 2); }
     for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
+    // recv (rank 0): one local arrival with the expected bytes per tile, the
+    // peers' st.async bytes complete it; free (ranks > 0): rank 0 arrives
+    // once per tile.
+    mbar_init(&recv_bar, 1);
+    mbar_init(&free_bar, 1);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -143,13 +200,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   pdl_launch();
   tc_fence_before();
   __syncthreads();
+  // Peers arrive on each other's barriers: all are initialised first.
+  if (p.ksplit > 1) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
   const int kblocks = p.K / kTcBK;
   const int kper = (kblocks + p.ksplit - 1) / p.ksplit;   // K blocks per split
   const int nunits = p.ntiles * p.ksplit;
 
-  if (threadIdx.x == 0) TC_STAMP(0);
+  if (threadIdx.x == 0) { TC_STAMP(0); TC_TL(0, globaltimer_ns()); }
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
     // Weights do not depend on the previous kernel: the W blocks of the first
@@ -267,12 +326,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int q = warp - 4;          // TMEM lane quarter = rows 32q .. 32q+31
     const int row = 32 * q + lane;
     float* tile = comb;              // [64][kTcCombStride]: lo half, then the final tile
-    __shared__ int last_flag;
     pdl_wait();                      // epilogues read the previous kernel's outputs
+    if (threadIdx.x == 128) { TC_STAMP(3); TC_TL(1, globaltimer_ns()); }
     int i = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
       const int t = u / p.ksplit, sp = u % p.ksplit;
       const int buf = i & 1;
+      // Split K, ranks > 0: rank 0 must have read this CTA's previous partial
+      // before the receive buffer is rewritten.
+      if (p.ksplit > 1 && sp != 0 && i > 0 &&
+          bar_any(2, 128, !tc_wait_cl(&free_bar, (uint32_t)(i - 1) & 1u, p, &abort_flag)))
+        break;
+      // Side inputs of this tile's epilogue, fetched while the MMAs run
+      // (the previous tile's epilogue is done with the region: loop-end
+      // barrier).  Visible to all epilogue threads after the barrier below.
+      if (sp == 0) {
+        const int e = threadIdx.x - 128;
+        if (p.ksplit > 1 && e == 0)
+          mbar_arrive_expect_tx(&recv_bar, (uint32_t)((p.ksplit - 1) * 64 * 64 * 4));
+        if constexpr (W8) {
+          if (e < 64) {
+            int r0, r1;
+            tc_tile_rows(p, t, r0, r1);
+            pre[e] = __ldg(p.wscale + (e < 32 ? r0 + e : r1 + e - 32));
+          }
+        }
+        Epi::prefetch(ep, t, pre + 64, e);
+      }
       // All four epilogue warps leave together (they share named barriers).
       if (bar_any(2, 128, !tc_wait(&tfull[buf], ((uint32_t)i >> 1) & 1u, p, &abort_flag))) break;
       if (threadIdx.x == 128) TC_STAMP(31);
@@ -294,72 +374,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
       if (q >= 2) {
+        float4* tr = reinterpret_cast<float4*>(tile + (row - 64) * kTcCombStride);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) tile[(row - 64) * kTcCombStride + c] = v[c];
+        for (int c = 0; c < 16; ++c) tr[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (threadIdx.x == 128) TC_STAMP(32);
       bool do_epi = true;
       if (q < 2) {
+        float4* tr = reinterpret_cast<float4*>(tile + row * kTcCombStride);
 #pragma unroll
-        for (int c = 0; c < 64; ++c) v[c] += tile[row * kTcCombStride + c];
-        if (p.ksplit > 1) {
-          // Split K: publish this part, take a ticket; the last part's CTA
-          // sums all parts in split order (deterministic) and finishes.
-          float* wsr = p.ws + (((size_t)t * p.ksplit + sp) * 64 + row) * 64;
+        for (int c = 0; c < 16; ++c) {
+          const float4 lo = tr[c];
+          v[4 * c] += lo.x; v[4 * c + 1] += lo.y; v[4 * c + 2] += lo.z; v[4 * c + 3] += lo.w;
+        }
+        if (p.ksplit > 1 && sp != 0) {
+          // Split K, ranks > 0: this row of the partial goes to rank 0.
+          const uint32_t dst = mapa_shared(smem_u32(recv + ((sp - 1) * 64 + row) * kTcCombStride), 0);
+          const uint32_t bar = mapa_shared(smem_u32(&recv_bar), 0);
 #pragma unroll
-          for (int c = 0; c < 64; c += 4) __stcg(reinterpret_cast<float4*>(wsr + c), make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]));
-          __threadfence();
-          asm volatile("bar.sync 3, 64;" ::: "memory");
-          if (row == 0) {
-            const int old = atomicAdd(p.counters + t, 1);
-            last_flag = (old == p.ksplit - 1);
-            if (old == p.ksplit - 1) p.counters[t] = 0;
-          }
-          asm volatile("bar.sync 3, 64;" ::: "memory");
-          if (threadIdx.x == 128) TC_STAMP(33);
+          for (int c = 0; c < 16; ++c)
+            st_async_f32x4(dst + 16 * c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]), bar);
         }
       }
       if (p.ksplit > 1) {
-        // The last part's CTA sums all parts in split order (deterministic)
-        // with all 128 epilogue threads, each half a row, every load of all
-        // parts in flight at once (one L2 round trip per 4 parts), and hands
-        // the rows to their owners through shared memory.
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        do_epi = last_flag != 0;
+        do_epi = sp == 0;
         if (do_epi) {
-          __threadfence();
-          const int rr = 32 * (q & 1) + lane, c0 = 32 * (q >> 1);
-          float acc[32];
+          // Rank 0 adds the partials of ranks 1..S-1 to its own, in rank
+          // order, then frees the peers' slots.
+          if (bar_any(2, 128, !tc_wait(&recv_bar, (uint32_t)i & 1u, p, &abort_flag))) break;
+          if (threadIdx.x == 128) TC_STAMP(33);
+          if (q < 2) {
+            for (int k = 0; k < p.ksplit - 1; ++k) {
+              const float4* rr = reinterpret_cast<const float4*>(recv + (k * 64 + row) * kTcCombStride);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) acc[c] = 0.f;
-          for (int k0 = 0; k0 < p.ksplit; k0 += 4) {
-            float4 a[4][8];
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              if (k0 + kk < p.ksplit) {
-                const float* pr = p.ws + (((size_t)t * p.ksplit + k0 + kk) * 64 + rr) * 64 + c0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) a[kk][j] = __ldcg(reinterpret_cast<const float4*>(pr) + j);
+              for (int c = 0; c < 16; ++c) {
+                const float4 x = rr[c];
+                v[4 * c] += x.x; v[4 * c + 1] += x.y; v[4 * c + 2] += x.z; v[4 * c + 3] += x.w;
               }
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              if (k0 + kk < p.ksplit) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  acc[4 * j] += a[kk][j].x; acc[4 * j + 1] += a[kk][j].y;
-                  acc[4 * j + 2] += a[kk][j].z; acc[4 * j + 3] += a[kk][j].w;
-                }
-              }
+            }
           }
-#pragma unroll
-          for (int c = 0; c < 32; ++c) tile[rr * kTcCombStride + c0 + c] = acc[c];
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          const int e = threadIdx.x - 128;
+          if (e >= 1 && e < p.ksplit) mbar_arrive_remote(mapa_shared(smem_u32(&free_bar), (uint32_t)e));
           if (threadIdx.x == 128) TC_STAMP(36);
-        }
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (q < 2 && do_epi) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c) v[c] = tile[row * kTcCombStride + c];
         }
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
@@ -367,25 +425,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (q < 2 && do_epi) {
         if constexpr (W8) {
           // W = scale * e4m3: column c of the tile is W row r0 + c (c < 32)
-          // or r1 + c - 32.
-          int r0, r1;
-          tc_tile_rows(p, t, r0, r1);
+          // or r1 + c - 32 (scales prefetched to pre[c]).
 #pragma unroll
-          for (int c = 0; c < 64; ++c) v[c] *= __ldg(p.wscale + (c < 32 ? r0 + c : r1 + c - 32));
+          for (int c = 0; c < 64; ++c) v[c] *= pre[c];
         }
-        Epi::apply(ep, t, row, v);
+        Epi::apply(ep, t, row, v, pre + 64);
         if (threadIdx.x == 128) TC_STAMP(37);
         // Column phase: the row values go through shared memory so that
         // global writes are coalesced (lanes = consecutive columns).
         if constexpr (Epi::kCols) {
+          float4* tr = reinterpret_cast<float4*>(tile + row * kTcCombStride);
 #pragma unroll
-          for (int c = 0; c < 64; ++c) tile[row * kTcCombStride + c] = v[c];
+          for (int c = 0; c < 16; ++c) tr[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
         }
       }
       if constexpr (Epi::kCols) {
         // do_epi is the same for all 128 epilogue threads.
         asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (do_epi) Epi::cols(ep, t, tile, threadIdx.x - 128);
+        if (do_epi) Epi::cols(ep, t, tile, threadIdx.x - 128, pre + 64);
         if (threadIdx.x == 128) TC_STAMP(38);
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
@@ -393,7 +450,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) TC_STAMP(35);
+  // No CTA leaves while a peer may still read its shared memory or arrive on
+  // its barriers.
+  if (p.ksplit > 1) cluster_sync_all();
+  if (threadIdx.x == 0) { TC_STAMP(35); TC_TL(2, ~globaltimer_ns()); }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTcTmemCols);
@@ -457,18 +517,24 @@ inline cudaError_t tc_gemm_launch(const TcGemmParams& p, const typename Epi::Par
     if (e != cudaSuccess) return e;
     attr = true;
   }
+  if (p.ksplit < 1 || p.ksplit > kTcMaxSplit) return cudaErrorInvalidValue;
   const int units = p.ntiles * p.ksplit;
-  const int grid = units < max_ctas ? units : max_ctas;
+  const int cap = max_ctas / p.ksplit * p.ksplit;   // whole clusters
+  const int grid = units < cap ? units : cap;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = TcCfg<W8>::kSmem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = (unsigned)p.ksplit;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.ksplit > 1 ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Epi, W8>, p, ep);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();

@@ -119,3 +119,8 @@ def test_extension_argument_checks_without_a_device():
     assert L.megakernel_batch_init_ex(ctypes.c_void_p(16), arr, 310, 4, 64, -1) is None
     assert L.megakernel_tp_exchange_slots(None, None) == -1
     assert L.megakernel_tc_gemm_test_e4m3(None, 64, None, None, 1024, 1024, None, None) == -1
+    # split factor outside 1..4, or a split left without a K block
+    x, w, o = ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16)
+    assert L.megakernel_tc_gemm_test_split(x, 64, w, 1024, 1024, 5, o, None) == -1
+    assert L.megakernel_tc_gemm_test_split(x, 64, w, 1024, 1024, 0, o, None) == -1
+    assert L.megakernel_tc_gemm_test_split(x, 64, w, 128, 64, 3, o, None) == -1
