@@ -265,23 +265,24 @@ struct EpiResid {
     for (int c = 0; c < 32; c += 4) *reinterpret_cast<float4*>(dst + c) = __ldcg(reinterpret_cast<const float4*>(src + c));
   }
   __device__ __forceinline__ static void apply(const Params&, int, int, float (&)[64], const float*) {}
-  // 128 threads: column c = tid & 63 for rows 32 (tid >> 6) .. +31, then
-  // the per-row sum of squares on 64 threads.
-  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid, const float* pre) {
+  // 128 threads: column c = tid & 63 for every other row of [ra, rb), then
+  // the per-row sum of squares on one thread per row.
+  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid, const float* pre,
+                                              int ra, int rb) {
     const BatchDev& d = ep.d;
-    const int c = tid & 63, r0 = 32 * (tid >> 6);
+    const int c = tid & 63;
     const int col = 64 * t + c;
     const float g = pre[c];
-#pragma unroll
-    for (int r = 0; r < kBMax / 2; ++r) {
-      const float xn = pre[64 + 64 * (r0 + r) + c] + tile[(r0 + r) * kTcCombStride + c];
-      __stcg(d.x + (size_t)(r0 + r) * kBH + col, xn);
-      tile[(r0 + r) * kTcCombStride + c] = xn;
-      put_hilo(ep.a_next, kBH, r0 + r, col, g * xn);
+#pragma unroll 8
+    for (int r = ra + (tid >> 6); r < rb; r += 2) {
+      const float xn = pre[64 + 64 * r + c] + tile[r * kTcCombStride + c];
+      __stcg(d.x + (size_t)r * kBH + col, xn);
+      tile[r * kTcCombStride + c] = xn;
+      put_hilo(ep.a_next, kBH, r, col, g * xn);
     }
     asm volatile("bar.sync 2, 128;" ::: "memory");
-    if (tid < 64) {
-      const int row = tid;
+    if (tid < rb - ra) {
+      const int row = ra + tid;
       float ss = 0.f;
       const float4* tr = reinterpret_cast<const float4*>(tile + row * kTcCombStride);
 #pragma unroll 4
@@ -311,11 +312,12 @@ struct EpiSwiGLU {
     prefetch_inv_rms(ep.d.ssq, pre, e);
   }
   __device__ __forceinline__ static void apply(const Params&, int, int, float (&)[64], const float*) {}
-  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid, const float* pre) {
+  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid, const float* pre,
+                                              int ra, int rb) {
     const int c = tid & 31;
     const int batch = ep.d.batch;
 #pragma unroll 4
-    for (int r = tid >> 5; r < kBMax; r += 4) {
+    for (int r = ra + (tid >> 5); r < rb; r += 4) {
       const float rr = pre[r];
       const float gt = tile[r * kTcCombStride + c] * rr, up = tile[r * kTcCombStride + 32 + c] * rr;
       put_hilo(ep.d.a_h, kBI, r, 32 * t + c, r < batch ? gt / (1.f + expf(-gt)) * up : 0.f);

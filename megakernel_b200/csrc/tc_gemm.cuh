@@ -21,13 +21,15 @@
 //               memory (lanes = consecutive columns, so global writes are
 //               coalesced).
 // Split K (ksplit = S, 2..4): the S CTAs of one output tile form a
-// thread-block cluster (cluster rank = split index).  Ranks 1..S-1 push
-// their hi + lo partial tiles into rank 0's receive buffers with st.async
-// (distributed shared memory, completing on rank 0's "recv" mbarrier by
-// byte count, so no release fence is needed); rank 0 adds them to its own
-// partial in rank order (deterministic), frees the buffers with a remote
-// arrive on each peer's "free" mbarrier and runs the epilogue.  No partial
-// crosses L2 and no counter is needed.
+// thread-block cluster (cluster rank = split index) and reduce-scatter their
+// hi + lo partial tiles: rank k owns rows [64k/S, 64(k+1)/S) of the tile;
+// every rank pushes the rows it does not own to their owners' receive
+// buffers with st.async (distributed shared memory, completing on the
+// owner's "recv" mbarrier by byte count, so no release fence is needed),
+// sums its own rows over the S partials in rank order (deterministic), frees
+// its buffers with a remote arrive on every peer's "free" mbarrier and runs
+// the epilogue for its rows.  No partial crosses L2 and no counter is
+// needed.
 // Every wait is bounded (timeout_ns); on expiry the kernel records
 // MK_ERR_TIMEOUT in *err and every role leaves its loop.
 #pragma once
@@ -187,11 +189,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); mbar_init(&conv[s], 2); }
     for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
-    // recv (rank 0): one local arrival with the expected bytes per tile, the
-    // peers' st.async bytes complete it; free (ranks > 0): rank 0 arrives
-    // once per tile.
+    // recv: one local arrival with the expected bytes per tile, the peers'
+    // st.async bytes complete it; free: every peer arrives once per tile
+    // when it has read its receive buffers.
     mbar_init(&recv_bar, 1);
-    mbar_init(&free_bar, 1);
+    mbar_init(&free_bar, p.ksplit > 1 ? p.ksplit - 1 : 1);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -330,20 +332,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 128) { TC_STAMP(3); TC_TL(1, globaltimer_ns()); }
     int i = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
-      const int t = u / p.ksplit, sp = u % p.ksplit;
+      const int S = p.ksplit, t = u / S, sp = u % S;
       const int buf = i & 1;
-      // Split K, ranks > 0: rank 0 must have read this CTA's previous partial
-      // before the receive buffer is rewritten.
-      if (p.ksplit > 1 && sp != 0 && i > 0 &&
-          bar_any(2, 128, !tc_wait_cl(&free_bar, (uint32_t)(i - 1) & 1u, p, &abort_flag)))
+      const int ra = 64 * sp / S, rb = 64 * (sp + 1) / S;   // rows this CTA finishes
+      // Split K: every peer must have read this CTA's previous rows before
+      // they are rewritten in its receive buffers.
+      if (S > 1 && i > 0 && bar_any(2, 128, !tc_wait_cl(&free_bar, (uint32_t)(i - 1) & 1u, p, &abort_flag)))
         break;
       // Side inputs of this tile's epilogue, fetched while the MMAs run
       // (the previous tile's epilogue is done with the region: loop-end
       // barrier).  Visible to all epilogue threads after the barrier below.
-      if (sp == 0) {
+      {
         const int e = threadIdx.x - 128;
-        if (p.ksplit > 1 && e == 0)
-          mbar_arrive_expect_tx(&recv_bar, (uint32_t)((p.ksplit - 1) * 64 * 64 * 4));
+        if (S > 1 && e == 0) mbar_arrive_expect_tx(&recv_bar, (uint32_t)((S - 1) * (rb - ra) * 64 * 4));
         if constexpr (W8) {
           if (e < 64) {
             int r0, r1;
@@ -380,7 +381,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (threadIdx.x == 128) TC_STAMP(32);
-      bool do_epi = true;
       if (q < 2) {
         float4* tr = reinterpret_cast<float4*>(tile + row * kTcCombStride);
 #pragma unroll
@@ -388,41 +388,55 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const float4 lo = tr[c];
           v[4 * c] += lo.x; v[4 * c + 1] += lo.y; v[4 * c + 2] += lo.z; v[4 * c + 3] += lo.w;
         }
-        if (p.ksplit > 1 && sp != 0) {
-          // Split K, ranks > 0: this row of the partial goes to rank 0.
-          const uint32_t dst = mapa_shared(smem_u32(recv + ((sp - 1) * 64 + row) * kTcCombStride), 0);
-          const uint32_t bar = mapa_shared(smem_u32(&recv_bar), 0);
+        if (S > 1 && (row < ra || row >= rb)) {
+          // Split K: a row another rank owns goes to slot (this rank's index
+          // among the owner's peers) of the owner's receive buffers.
+          int dest = 0;
+          while (dest + 1 < S && row >= 64 * (dest + 1) / S) ++dest;
+          const int slot = sp < dest ? sp : sp - 1;
+          const uint32_t dst = mapa_shared(smem_u32(recv + (slot * 64 + row) * kTcCombStride), (uint32_t)dest);
+          const uint32_t bar = mapa_shared(smem_u32(&recv_bar), (uint32_t)dest);
 #pragma unroll
           for (int c = 0; c < 16; ++c)
             st_async_f32x4(dst + 16 * c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]), bar);
         }
       }
-      if (p.ksplit > 1) {
-        do_epi = sp == 0;
-        if (do_epi) {
-          // Rank 0 adds the partials of ranks 1..S-1 to its own, in rank
-          // order, then frees the peers' slots.
-          if (bar_any(2, 128, !tc_wait(&recv_bar, (uint32_t)i & 1u, p, &abort_flag))) break;
-          if (threadIdx.x == 128) TC_STAMP(33);
-          if (q < 2) {
-            for (int k = 0; k < p.ksplit - 1; ++k) {
-              const float4* rr = reinterpret_cast<const float4*>(recv + (k * 64 + row) * kTcCombStride);
+      if (S > 1) {
+        // Own rows: the S partials summed in rank order (this rank's own
+        // partial at position sp), then every peer is told that its rows
+        // have been read.
+        if (bar_any(2, 128, !tc_wait(&recv_bar, (uint32_t)i & 1u, p, &abort_flag))) break;
+        if (threadIdx.x == 128) TC_STAMP(33);
+        if (q < 2 && row >= ra && row < rb) {
+          float4 acc[16];
+          const float4* r0p = reinterpret_cast<const float4*>(recv + row * kTcCombStride);
 #pragma unroll
-              for (int c = 0; c < 16; ++c) {
-                const float4 x = rr[c];
-                v[4 * c] += x.x; v[4 * c + 1] += x.y; v[4 * c + 2] += x.z; v[4 * c + 3] += x.w;
-              }
+          for (int c = 0; c < 16; ++c)
+            acc[c] = sp == 0 ? make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]) : r0p[c];
+          for (int j = 1; j < S; ++j) {
+            const float4* rj = reinterpret_cast<const float4*>(recv + ((j < sp ? j : j - 1) * 64 + row) * kTcCombStride);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const float4 x = j == sp ? make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]) : rj[c];
+              acc[c].x += x.x; acc[c].y += x.y; acc[c].z += x.z; acc[c].w += x.w;
             }
           }
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-          const int e = threadIdx.x - 128;
-          if (e >= 1 && e < p.ksplit) mbar_arrive_remote(mapa_shared(smem_u32(&free_bar), (uint32_t)e));
-          if (threadIdx.x == 128) TC_STAMP(36);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            v[4 * c] = acc[c].x; v[4 * c + 1] = acc[c].y; v[4 * c + 2] = acc[c].z; v[4 * c + 3] = acc[c].w;
+          }
         }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        // Arrivals come from the lo-half warps, which issued no st.async: a
+        // release by a thread with stores in flight to another CTA waits for
+        // them (measured ~1-2 us).
+        const int e = threadIdx.x - 192;
+        if (e >= 0 && e < S - 1) mbar_arrive_remote(mapa_shared(smem_u32(&free_bar), (uint32_t)(e < sp ? e : e + 1)));
+        if (threadIdx.x == 128) TC_STAMP(36);
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
       if (threadIdx.x == 128) TC_STAMP(34);
-      if (q < 2 && do_epi) {
+      if (q < 2 && row >= ra && row < rb) {
         if constexpr (W8) {
           // W = scale * e4m3: column c of the tile is W row r0 + c (c < 32)
           // or r1 + c - 32 (scales prefetched to pre[c]).
@@ -440,9 +454,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       if constexpr (Epi::kCols) {
-        // do_epi is the same for all 128 epilogue threads.
         asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (do_epi) Epi::cols(ep, t, tile, threadIdx.x - 128, pre + 64);
+        Epi::cols(ep, t, tile, threadIdx.x - 128, pre + 64, ra, rb);
         if (threadIdx.x == 128) TC_STAMP(38);
       }
       asm volatile("bar.sync 2, 128;" ::: "memory");
