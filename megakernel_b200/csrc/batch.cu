@@ -31,6 +31,8 @@ __global__ void hilo_split_kernel(const float* __restrict__ x, int rows, int K, 
 // Plain epilogue: out[seq][64 t + c] = v[c] for seq < rows.
 struct EpiStore {
   static constexpr bool kCols = false;
+  // Prefetched inputs are the same for every tile.
+  static constexpr bool kPrePerTile = false;
   static constexpr int kPre = 0;
   struct Params {
     float* out;
@@ -154,6 +156,8 @@ __global__ void bembed_kernel(BatchDev d, const __nv_bfloat16* __restrict__ emb,
 // sequence's position, writes q (fp32) or appends K / V (bf16) to the cache.
 struct EpiQKV {
   static constexpr bool kCols = false;
+  // Prefetched inputs depend on the tile index (re-fetched per 64-column tile).
+  static constexpr bool kPrePerTile = true;
   // pre: [0, 64) 1/rms per row, [64, 128) head-norm gains, [128, 192) the
   // row's position (int bits), then [192 + 64 r, +64) cos | sin of row r.
   static constexpr int kPre = 3 * 64 + 64 * 64;
@@ -245,6 +249,8 @@ struct EpiQKV {
 // then thread = column again: hi/lo of (g . x) into a_next.
 struct EpiResid {
   static constexpr bool kCols = true;
+  // Prefetched inputs depend on the tile index (re-fetched per 64-column tile).
+  static constexpr bool kPrePerTile = true;
   // pre: [0, 64) gains of the tile's columns, then x[r][64 t + c] at
   // 64 + 64 r + c (the residual stream's tile, fetched during the MMAs).
   static constexpr int kPre = 64 + 64 * 64;
@@ -304,6 +310,8 @@ struct EpiResid {
 // (up / rms), then hi/lo of h into a_h.
 struct EpiSwiGLU {
   static constexpr bool kCols = true;
+  // Prefetched inputs depend on the tile index (re-fetched per 64-column tile).
+  static constexpr bool kPrePerTile = true;
   static constexpr int kPre = 64;   // 1 / rms per row
   struct Params {
     BatchDev d;
@@ -329,6 +337,8 @@ struct EpiSwiGLU {
 // (value, lowest index) of the tile -> lm_part[t][seq]; optional logits.
 struct EpiArgmax {
   static constexpr bool kCols = false;
+  // Prefetched inputs are the same for every tile.
+  static constexpr bool kPrePerTile = false;
   static constexpr int kPre = 64;   // 1 / rms per row
   struct Params {
     BatchDev d;
@@ -1160,9 +1170,18 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
              EpiResid::Params{d, d.a_x, g_next}, 4 * l + 3) != cudaSuccess)
       return ::MK_ERR_LAUNCH;
   }
-  if (gemm(Tag<EpiArgmax>{}, gemm_params(d, M + kMapAx, M + map_lm(), kBH, kBLMTiles, 0, 1),
-           EpiArgmax::Params{d, logits}, 4 * kBL) != cudaSuccess)
-    return ::MK_ERR_LAUNCH;
+  // LM head: bf16 weights in CTA tiles of 4 x 64 columns (the activation
+  // operand is re-read a quarter as often); e4m3 weights in 64-column tiles.
+  {
+    TcGemmParams p = gemm_params(d, M + kMapAx, M + map_lm(), kBH, kBLMTiles, 0, 1);
+    const EpiArgmax::Params ep{d, logits};
+#if MK_TC_STAMPS
+    p.tl = tl_next++;
+#endif
+    const cudaError_t e = w8 ? (p.wscale = s->wsc + s->sc_off[4 * kBL], tc_gemm_launch<EpiArgmax, true>(p, ep, s->sms, st))
+                             : tc_gemm_launch<EpiArgmax, false, 4>(p, ep, s->sms, st);
+    if (e != cudaSuccess) return ::MK_ERR_LAUNCH;
+  }
   if (launch_pdl(bargmax_kernel, s->batch, 256, 0, st, d, out) != cudaSuccess) return ::MK_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? ::MK_OK : ::MK_ERR_LAUNCH;
 }

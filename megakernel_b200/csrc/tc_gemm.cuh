@@ -63,17 +63,26 @@ constexpr int kTcRecvFloats = (kTcMaxSplit - 1) * 64 * kTcCombStride;
 // Per-instance ring: 5 stages of A + W (measured on B200: 4 to 8 stages give
 // the same step time); with e4m3 weights (W8) each stage also holds the 4 KB
 // e4m3 W block that two converter warps expand into the bf16 W tile.
-template <bool W8>
+// NSUB = 4 (bf16 weights, no split K; the LM head): a CTA tile is 4 x 64 =
+// 256 output columns, so each stage carries 32 KB of W against the same
+// 16 KB of A and the activation operand is re-read a quarter as often; 4
+// stages, two 256-column TMEM accumulators, the epilogue runs once per
+// 64-column sub-tile.
+template <bool W8, int NSUB = 1>
 struct TcCfg {
-  static constexpr int kStages = kTcStages;
+  static_assert(NSUB == 1 || (NSUB == 4 && !W8), "wide tiles: bf16 weights only");
+  static constexpr int kStages = NSUB == 1 ? kTcStages : 4;
   static constexpr int kW8Bytes = W8 ? kTcBN * kTcBK : 0;
-  static constexpr int kStageBytes = kTcStageBytes + kW8Bytes;
-  static constexpr uint32_t kTxBytes = W8 ? kTcABytes + kW8Bytes : kTcStageBytes;
-  static constexpr size_t kSmem =
-      1024 + (size_t)kStages * kStageBytes + 64 * kTcCombStride * 4 + (size_t)kTcPreFloats * 4 +
-      (size_t)kTcRecvFloats * 4;
+  static constexpr int kWBytes = NSUB * kTcWBytes;            // bf16 W tile
+  static constexpr int kStageBytes = kTcABytes + kWBytes + kW8Bytes;
+  static constexpr uint32_t kTxBytes = W8 ? kTcABytes + kW8Bytes : kTcABytes + kWBytes;
+  static constexpr uint32_t kTmemCols = 2 * 64 * NSUB;        // two accumulators
+  // Prefetch region: wide tiles only take epilogues with small side inputs.
+  static constexpr int kPreFloats = NSUB == 1 ? kTcPreFloats : 256;
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 64 * kTcCombStride * 4 +
+                                  (size_t)kPreFloats * 4 + (NSUB == 1 ? (size_t)kTcRecvFloats * 4 : 0);
+  static_assert(kSmem + 1024 <= 232448, "shared memory (dynamic + static) per CTA");
 };
-constexpr uint32_t kTcTmemCols = 128;                 // two 64-column accumulators
 
 struct TcGemmParams {
   const CUtensorMap* amap;  // A [128 x K] bf16, box {64, 128}, SW128
@@ -170,16 +179,17 @@ __device__ __forceinline__ uint32_t tc_e4m3x2_to_bf16x2(uint16_t v) {
   return *reinterpret_cast<const uint32_t*>(&b);
 }
 
-template <class Epi, bool W8 = false>
+template <class Epi, bool W8 = false, int NSUB = 1>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_kernel(const __grid_constant__ TcGemmParams p, const __grid_constant__ typename Epi::Params ep) {
-  using C = TcCfg<W8>;
+  using C = TcCfg<W8, NSUB>;
+  static_assert(NSUB == 1 || !Epi::kPrePerTile, "wide tiles prefetch once per CTA tile");
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
   float* comb = reinterpret_cast<float*>(smem + (size_t)C::kStages * C::kStageBytes);
   float* pre = comb + 64 * kTcCombStride;
-  float* recv = pre + kTcPreFloats;        // split K, rank 0: partials of ranks 1..S-1 [S-1][64][kTcCombStride]
-  static_assert(Epi::kPre <= kTcPreFloats - 64, "epilogue prefetch region");
+  float* recv = pre + C::kPreFloats;       // split K: partial rows from the peers [S-1][64][kTcCombStride]
+  static_assert(Epi::kPre <= C::kPreFloats - 64, "epilogue prefetch region");
   __shared__ alignas(8) uint64_t full[kTcStages], empty[kTcStages], conv[kTcStages], tfull[2], tempty[2];
   __shared__ alignas(8) uint64_t recv_bar, free_bar;   // split K (cluster) only
   __shared__ uint32_t tmem_base_sh;
@@ -197,7 +207,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) { tmem_alloc(&tmem_base_sh, kTcTmemCols); tmem_relinquish(); }
+  if (warp == 1) { tmem_alloc(&tmem_base_sh, C::kTmemCols); tmem_relinquish(); }
   if (warp == 0 && lane == 0) { prefetch_tmap(p.amap); prefetch_tmap(p.wmap); }
   pdl_launch();
   tc_fence_before();
@@ -208,7 +218,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = tmem_base_sh;
   const int kblocks = p.K / kTcBK;
   const int kper = (kblocks + p.ksplit - 1) / p.ksplit;   // K blocks per split
-  const int nunits = p.ntiles * p.ksplit;
+  const int nct = (p.ntiles + NSUB - 1) / NSUB;           // CTA tiles (NSUB 64-column sub-tiles each)
+  const int nunits = nct * p.ksplit;
 
   if (threadIdx.x == 0) { TC_STAMP(0); TC_TL(0, globaltimer_ns()); }
   if (warp == 0 && lane == 0) {
@@ -229,10 +240,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_arrive_expect_tx(&full[j], C::kTxBytes);
         // bf16 W: the two 32-row halves of the SW128 tile; e4m3 W: the two
         // halves of the staging block after the tile (64 bytes per row).
-        uint8_t* wdst = W8 ? st + kTcABytes + kTcWBytes : st + kTcABytes;
-        const int half = W8 ? C::kW8Bytes / 2 : kTcWBytes / 2;
-        tma_load_2d(wdst, p.wmap, kb * kTcBK, r0, &full[j]);
-        tma_load_2d(wdst + half, p.wmap, kb * kTcBK, r1, &full[j]);
+        if constexpr (NSUB > 1) {
+          for (int k = 0; k < 2 * NSUB; ++k) tma_load_2d(st + kTcABytes + 4096 * k, p.wmap, kb * kTcBK, 64 * NSUB * t + 32 * k, &full[j]);
+        } else {
+          uint8_t* wdst = W8 ? st + kTcABytes + kTcWBytes : st + kTcABytes;
+          const int half = W8 ? C::kW8Bytes / 2 : kTcWBytes / 2;
+          tma_load_2d(wdst, p.wmap, kb * kTcBK, r0, &full[j]);
+          tma_load_2d(wdst + half, p.wmap, kb * kTcBK, r1, &full[j]);
+        }
       }
     }
     TC_STAMP(1);
@@ -252,10 +267,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (!tc_wait(&empty[s], ph ^ 1u, p, &abort_flag)) goto done_producer;
           mbar_arrive_expect_tx(&full[s], C::kTxBytes);
           tma_load_2d(st, p.amap, kb * kTcBK, 0, &full[s]);
-          uint8_t* wdst = W8 ? st + kTcABytes + kTcWBytes : st + kTcABytes;
-          const int half = W8 ? C::kW8Bytes / 2 : kTcWBytes / 2;
-          tma_load_2d(wdst, p.wmap, kb * kTcBK, r0, &full[s]);
-          tma_load_2d(wdst + half, p.wmap, kb * kTcBK, r1, &full[s]);
+          if constexpr (NSUB > 1) {
+            for (int k = 0; k < 2 * NSUB; ++k) tma_load_2d(st + kTcABytes + 4096 * k, p.wmap, kb * kTcBK, 64 * NSUB * t + 32 * k, &full[s]);
+          } else {
+            uint8_t* wdst = W8 ? st + kTcABytes + kTcWBytes : st + kTcABytes;
+            const int half = W8 ? C::kW8Bytes / 2 : kTcWBytes / 2;
+            tma_load_2d(wdst, p.wmap, kb * kTcBK, r0, &full[s]);
+            tma_load_2d(wdst + half, p.wmap, kb * kTcBK, r1, &full[s]);
+          }
         }
         if (++s == C::kStages) { s = 0; ph ^= 1u; }
       }
@@ -263,7 +282,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   done_producer:;
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
-    constexpr uint32_t idesc = tc_idesc_bf16(kTcBM, kTcBN);
+    constexpr uint32_t idesc = tc_idesc_bf16(kTcBM, kTcBN * NSUB);
     uint32_t s = 0, ph = 0;
     int i = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++i) {
@@ -272,7 +291,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int buf = i & 1;
       if (!tc_wait(&tempty[buf], (((uint32_t)i >> 1) & 1u) ^ 1u, p, &abort_flag)) break;
       tc_fence_after();
-      const uint32_t d = tmem + (uint32_t)(buf * kTcBN);
+      const uint32_t d = tmem + (uint32_t)(buf * kTcBN * NSUB);
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc_wait(W8 ? &conv[s] : &full[s], ph, p, &abort_flag)) { ok = false; break; }
@@ -358,107 +377,113 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (bar_any(2, 128, !tc_wait(&tfull[buf], ((uint32_t)i >> 1) & 1u, p, &abort_flag))) break;
       if (threadIdx.x == 128) TC_STAMP(31);
       tc_fence_after();
-      float v[64];
-      {
-        uint32_t r[32];
-        const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTcBN);
-        tmem_ld_32x32b_x32(ta, r);
-        tmem_ld_wait();
+      bool quit = false;
+      // NSUB 64-column sub-tiles of the accumulator (sub-tile tt = t NSUB + h).
+      for (int h = 0; h < NSUB; ++h) {
+        const int tt = t * NSUB + h;
+        float v[64];
+        {
+          uint32_t r[32];
+          const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * kTcBN * NSUB + 64 * h);
+          tmem_ld_32x32b_x32(ta, r);
+          tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
-        tmem_ld_32x32b_x32(ta + 32, r);
-        tmem_ld_wait();
+          for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
+          tmem_ld_32x32b_x32(ta + 32, r);
+          tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) v[32 + c] = __uint_as_float(r[c]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
-      if (q >= 2) {
-        float4* tr = reinterpret_cast<float4*>(tile + (row - 64) * kTcCombStride);
-#pragma unroll
-        for (int c = 0; c < 16; ++c) tr[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-      }
-      asm volatile("bar.sync 2, 128;" ::: "memory");
-      if (threadIdx.x == 128) TC_STAMP(32);
-      if (q < 2) {
-        float4* tr = reinterpret_cast<float4*>(tile + row * kTcCombStride);
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const float4 lo = tr[c];
-          v[4 * c] += lo.x; v[4 * c + 1] += lo.y; v[4 * c + 2] += lo.z; v[4 * c + 3] += lo.w;
+          for (int c = 0; c < 32; ++c) v[32 + c] = __uint_as_float(r[c]);
         }
-        if (S > 1 && (row < ra || row >= rb)) {
-          // Split K: a row another rank owns goes to slot (this rank's index
-          // among the owner's peers) of the owner's receive buffers.
-          int dest = 0;
-          while (dest + 1 < S && row >= 64 * (dest + 1) / S) ++dest;
-          const int slot = sp < dest ? sp : sp - 1;
-          const uint32_t dst = mapa_shared(smem_u32(recv + (slot * 64 + row) * kTcCombStride), (uint32_t)dest);
-          const uint32_t bar = mapa_shared(smem_u32(&recv_bar), (uint32_t)dest);
-#pragma unroll
-          for (int c = 0; c < 16; ++c)
-            st_async_f32x4(dst + 16 * c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]), bar);
-        }
-      }
-      if (S > 1) {
-        // Own rows: the S partials summed in rank order (this rank's own
-        // partial at position sp), then every peer is told that its rows
-        // have been read.
-        if (bar_any(2, 128, !tc_wait(&recv_bar, (uint32_t)i & 1u, p, &abort_flag))) break;
-        if (threadIdx.x == 128) TC_STAMP(33);
-        if (q < 2 && row >= ra && row < rb) {
-          float4 acc[16];
-          const float4* r0p = reinterpret_cast<const float4*>(recv + row * kTcCombStride);
-#pragma unroll
-          for (int c = 0; c < 16; ++c)
-            acc[c] = sp == 0 ? make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]) : r0p[c];
-          for (int j = 1; j < S; ++j) {
-            const float4* rj = reinterpret_cast<const float4*>(recv + ((j < sp ? j : j - 1) * 64 + row) * kTcCombStride);
-#pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              const float4 x = j == sp ? make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]) : rj[c];
-              acc[c].x += x.x; acc[c].y += x.y; acc[c].z += x.z; acc[c].w += x.w;
-            }
-          }
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            v[4 * c] = acc[c].x; v[4 * c + 1] = acc[c].y; v[4 * c + 2] = acc[c].z; v[4 * c + 3] = acc[c].w;
-          }
-        }
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        // Arrivals come from the lo-half warps, which issued no st.async: a
-        // release by a thread with stores in flight to another CTA waits for
-        // them (measured ~1-2 us).
-        const int e = threadIdx.x - 192;
-        if (e >= 0 && e < S - 1) mbar_arrive_remote(mapa_shared(smem_u32(&free_bar), (uint32_t)(e < sp ? e : e + 1)));
-        if (threadIdx.x == 128) TC_STAMP(36);
-      }
-      asm volatile("bar.sync 2, 128;" ::: "memory");
-      if (threadIdx.x == 128) TC_STAMP(34);
-      if (q < 2 && row >= ra && row < rb) {
-        if constexpr (W8) {
-          // W = scale * e4m3: column c of the tile is W row r0 + c (c < 32)
-          // or r1 + c - 32 (scales prefetched to pre[c]).
-#pragma unroll
-          for (int c = 0; c < 64; ++c) v[c] *= pre[c];
-        }
-        Epi::apply(ep, t, row, v, pre + 64);
-        if (threadIdx.x == 128) TC_STAMP(37);
-        // Column phase: the row values go through shared memory so that
-        // global writes are coalesced (lanes = consecutive columns).
-        if constexpr (Epi::kCols) {
-          float4* tr = reinterpret_cast<float4*>(tile + row * kTcCombStride);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0 && h == NSUB - 1) mbar_arrive(&tempty[buf]);
+        if (q >= 2) {
+          float4* tr = reinterpret_cast<float4*>(tile + (row - 64) * kTcCombStride);
 #pragma unroll
           for (int c = 0; c < 16; ++c) tr[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
         }
-      }
-      if constexpr (Epi::kCols) {
         asm volatile("bar.sync 2, 128;" ::: "memory");
-        Epi::cols(ep, t, tile, threadIdx.x - 128, pre + 64, ra, rb);
-        if (threadIdx.x == 128) TC_STAMP(38);
+        if (threadIdx.x == 128) TC_STAMP(32);
+        if (q < 2) {
+          float4* tr = reinterpret_cast<float4*>(tile + row * kTcCombStride);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const float4 lo = tr[c];
+            v[4 * c] += lo.x; v[4 * c + 1] += lo.y; v[4 * c + 2] += lo.z; v[4 * c + 3] += lo.w;
+          }
+          if (S > 1 && (row < ra || row >= rb)) {
+            // Split K: a row another rank owns goes to slot (this rank's index
+            // among the owner's peers) of the owner's receive buffers.
+            int dest = 0;
+            while (dest + 1 < S && row >= 64 * (dest + 1) / S) ++dest;
+            const int slot = sp < dest ? sp : sp - 1;
+            const uint32_t dst = mapa_shared(smem_u32(recv + (slot * 64 + row) * kTcCombStride), (uint32_t)dest);
+            const uint32_t bar = mapa_shared(smem_u32(&recv_bar), (uint32_t)dest);
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              st_async_f32x4(dst + 16 * c, make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]), bar);
+          }
+        }
+        if (S > 1) {
+          // Own rows: the S partials summed in rank order (this rank's own
+          // partial at position sp), then every peer is told that its rows
+          // have been read.
+          if (bar_any(2, 128, !tc_wait(&recv_bar, (uint32_t)i & 1u, p, &abort_flag))) { quit = true; break; }
+          if (threadIdx.x == 128) TC_STAMP(33);
+          if (q < 2 && row >= ra && row < rb) {
+            float4 acc[16];
+            const float4* r0p = reinterpret_cast<const float4*>(recv + row * kTcCombStride);
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              acc[c] = sp == 0 ? make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]) : r0p[c];
+            for (int j = 1; j < S; ++j) {
+              const float4* rj = reinterpret_cast<const float4*>(recv + ((j < sp ? j : j - 1) * 64 + row) * kTcCombStride);
+#pragma unroll
+              for (int c = 0; c < 16; ++c) {
+                const float4 x = j == sp ? make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]) : rj[c];
+                acc[c].x += x.x; acc[c].y += x.y; acc[c].z += x.z; acc[c].w += x.w;
+              }
+            }
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              v[4 * c] = acc[c].x; v[4 * c + 1] = acc[c].y; v[4 * c + 2] = acc[c].z; v[4 * c + 3] = acc[c].w;
+            }
+          }
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          // Arrivals come from the lo-half warps, which issued no st.async: a
+          // release by a thread with stores in flight to another CTA waits for
+          // them (measured ~1-2 us).
+          const int e = threadIdx.x - 192;
+          if (e >= 0 && e < S - 1) mbar_arrive_remote(mapa_shared(smem_u32(&free_bar), (uint32_t)(e < sp ? e : e + 1)));
+          if (threadIdx.x == 128) TC_STAMP(36);
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (threadIdx.x == 128) TC_STAMP(34);
+        if (q < 2 && row >= ra && row < rb && tt < p.ntiles) {
+          if constexpr (W8) {
+            // W = scale * e4m3: column c of the tile is W row r0 + c (c < 32)
+            // or r1 + c - 32 (scales prefetched to pre[c]).
+#pragma unroll
+            for (int c = 0; c < 64; ++c) v[c] *= pre[c];
+          }
+          Epi::apply(ep, tt, row, v, pre + 64);
+          if (threadIdx.x == 128) TC_STAMP(37);
+          // Column phase: the row values go through shared memory so that
+          // global writes are coalesced (lanes = consecutive columns).
+          if constexpr (Epi::kCols) {
+            float4* tr = reinterpret_cast<float4*>(tile + row * kTcCombStride);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) tr[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+          }
+        }
+        if constexpr (Epi::kCols) {
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          Epi::cols(ep, tt, tile, threadIdx.x - 128, pre + 64, ra, rb);
+          if (threadIdx.x == 128) TC_STAMP(38);
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
       }
-      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (quit) break;
     }
   }
   tc_fence_before();
@@ -469,7 +494,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) { TC_STAMP(35); TC_TL(2, ~globaltimer_ns()); }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTcTmemCols);
+    tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 
@@ -520,24 +545,24 @@ inline bool tc_make_map_e4m3(CUtensorMap* m, const void* base, uint64_t rows, ui
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <class Epi, bool W8 = false>
+template <class Epi, bool W8 = false, int NSUB = 1>
 inline cudaError_t tc_gemm_launch(const TcGemmParams& p, const typename Epi::Params& ep, int max_ctas,
                                   cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<Epi, W8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)TcCfg<W8>::kSmem);
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<Epi, W8, NSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)TcCfg<W8, NSUB>::kSmem);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  if (p.ksplit < 1 || p.ksplit > kTcMaxSplit) return cudaErrorInvalidValue;
-  const int units = p.ntiles * p.ksplit;
+  if (p.ksplit < 1 || p.ksplit > kTcMaxSplit || (NSUB > 1 && p.ksplit != 1)) return cudaErrorInvalidValue;
+  const int units = (p.ntiles + NSUB - 1) / NSUB * p.ksplit;
   const int cap = max_ctas / p.ksplit * p.ksplit;   // whole clusters
   const int grid = units < cap ? units : cap;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = TcCfg<W8>::kSmem;
+  cfg.dynamicSmemBytes = TcCfg<W8, NSUB>::kSmem;
   cfg.stream = st;
   cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -548,7 +573,7 @@ inline cudaError_t tc_gemm_launch(const TcGemmParams& p, const typename Epi::Par
   at[1].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = p.ksplit > 1 ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Epi, W8>, p, ep);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tc_gemm_kernel<Epi, W8, NSUB>, p, ep);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
