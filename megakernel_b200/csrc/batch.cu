@@ -57,7 +57,14 @@ constexpr int kBMax = 64;          // sequences per batch
 constexpr int kBH = 1024, kBQ = 1024, kBKV = 512, kBI = 2816, kBD = 64, kBNQ = 16, kBNKV = 8, kBL = 28;
 constexpr int kBV = 151936;
 constexpr int kBHT = kBH / 64;     // 64-column tiles of the residual stream (sum-of-squares partials)
-constexpr int kBChunk = 64;        // positions per attention work item (one warp)
+// Positions per attention chunk (K/V tile of a warp's pipeline).
+#ifndef MK_BATTN_CHUNK
+#define MK_BATTN_CHUNK 64
+#endif
+constexpr int kBChunk = MK_BATTN_CHUNK;
+static_assert(kBChunk == 32 || kBChunk == 64, "attention chunk");
+constexpr int kBNT = kBChunk / 8;      // 8-position n-tiles of a chunk (scores)
+constexpr int kBKS = kBChunk / 16;     // 16-position k-steps of a chunk (P.V)
 constexpr int kBLMTiles = kBV / 64;
 static_assert(kBV % 64 == 0, "vocab tiles");
 
@@ -391,7 +398,6 @@ constexpr int kBAttnWarps = 2;
 #define MK_BATTN_BUFS 3
 #endif
 constexpr int kBAttnBufs = MK_BATTN_BUFS;   // chunks of K/V per warp: current + in flight
-constexpr int kBAttnBlocksPerSm = kBAttnBufs == 2 ? 3 : 2;
 // bf16 cache: K/V chunks land swizzled in kBAttnBufs buffers.  fp8 cache
 // (e4m3): the chunks land unswizzled in kBAttnBufs staging buffers (4 KB
 // each) and are converted into one f16 working tile (swizzled) before use.
@@ -406,6 +412,7 @@ struct AttnWarpSmemT {
 };
 template <bool F8>
 constexpr size_t attn_smem_bytes() { return sizeof(AttnWarpSmemT<F8>) * kBAttnWarps; }
+
 
 __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   int old;
@@ -554,7 +561,7 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       if constexpr (F8) {
         const uint32_t ks = smem_u32(sw.k8[buf]), vs = smem_u32(sw.v8[buf]);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < kBChunk / 8; ++k) {
           const int idx = lane + 32 * k, row = idx >> 2, ch = idx & 3;
           const size_t src_row = (size_t)min(c * kBChunk + row, d.max_seq - 1);
           cp_async16(ks + (uint32_t)(row * 64 + ch * 16), d.kv8 + k_off + src_row * kBD + ch * 16);
@@ -563,7 +570,7 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       } else {
         const uint32_t ks = smem_u32(sw.k[buf]), vs = smem_u32(sw.v[buf]);
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
+        for (int k = 0; k < kBChunk / 4; ++k) {
           const int idx = lane + 32 * k, row = idx >> 3, ch = idx & 7;
           const size_t src_row = (size_t)min(c * kBChunk + row, d.max_seq - 1);
           cp_async16(ks + swz(row, ch), d.kv + k_off + src_row * kBD + ch * 8);
@@ -613,7 +620,7 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       if constexpr (F8) {
         // e4m3 -> f16 (exact) into the swizzled working tile.
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
+        for (int k = 0; k < kBChunk / 4; ++k) {
           const int idx = lane + 32 * k, row = idx >> 3, ch = idx & 7;
           const uint2 ka = *reinterpret_cast<const uint2*>(&sw.k8[buf][row * 64 + ch * 8]);
           const uint2 va = *reinterpret_cast<const uint2*>(&sw.v8[buf][row * 64 + ch * 8]);
@@ -631,13 +638,13 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       const uint32_t ks = smem_u32(sw.k[tb]), vs = smem_u32(sw.v[tb]);
       const int n = min(kBChunk, p + 1 - c * kBChunk);
       // S[16 x 64]: 8 n-tiles of 8 positions
-      float sacc[8][4];
+      float sacc[kBNT][4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f; }
+      for (int j = 0; j < kBNT; ++j) { sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f; }
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-        for (int jp = 0; jp < 4; ++jp) {
+        for (int jp = 0; jp < kBNT / 2; ++jp) {
           // matrices: (n-tile 2jp, k lo), (2jp, k hi), (2jp+1, k lo), (2jp+1, k hi)
           const int mi = lane >> 3, r = lane & 7;
           const int row = (2 * jp + (mi >> 1)) * 8 + r, ch = kk * 2 + (mi & 1);
@@ -651,10 +658,10 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       }
       // rows 0/1 (+ rows 2/3 from lane + 8): full scores of heads 0/1 in
       // lanes g = 0 / 1, positions 8j + 2tq, +1
-      float sc[8][2];
+      float sc[kBNT][2];
       float mx = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < kBNT; ++j) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float v = sacc[j][e] + __shfl_down_sync(0xffffffffu, sacc[j][e], 8);
@@ -667,7 +674,7 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       float ls = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < kBNT; ++j)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           sc[j][e] = expf(sc[j][e] - mx);
@@ -677,9 +684,9 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
       ls += __shfl_xor_sync(0xffffffffu, ls, 2);
       // P as A operand: lanes g = 0/1 give hi of their head, lanes g = 2/3 the
       // lo of lane - 8's probabilities, other rows zero.
-      uint32_t pa[4][2];
+      uint32_t pa[kBKS][2];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
+      for (int kk = 0; kk < kBKS; ++kk) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int j = 2 * kk + hh;
@@ -695,7 +702,7 @@ __global__ void __launch_bounds__(kBAttnWarps * 32) battn_kernel(BatchDev d, int
 #pragma unroll
       for (int j = 0; j < 8; ++j) { oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f; }
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
+      for (int kk = 0; kk < kBKS; ++kk) {
 #pragma unroll
         for (int jp = 0; jp < 4; ++jp) {
           // .trans matrices: (pos lo 8, dims 2jp), (pos hi 8, dims 2jp), (pos lo, 2jp+1), (pos hi, 2jp+1)
@@ -1096,13 +1103,6 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
   const CUtensorMap* M = s->maps;
   if (launch_pdl(bembed_kernel, kBMax, 256, 0, st, d, s->wp[0], s->wp[2], forced, prev_out) != cudaSuccess)
     return ::MK_ERR_LAUNCH;
-  const int attn_blocks = s->sms * kBAttnBlocksPerSm;   // 2-warp blocks, as many as fit per SM
-  // Chunks per attention item: split each (sequence, head) into as many
-  // spans as there are warp slots for all of them at once, at the
-  // engine's capacity; never more items than slots (a second wave of items
-  // would double the layer's attention time).
-  const int per_pair = std::max(1, s->sms * kBAttnBlocksPerSm * kBAttnWarps / (d.batch * kBNKV));
-  const int attn_span = (d.maxch + per_pair - 1) / per_pair;
   static bool attn_attr = false;
   if (!attn_attr) {
     if (cudaFuncSetAttribute(battn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1114,6 +1114,23 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
       return ::MK_ERR_LAUNCH;
     attn_attr = true;
   }
+  // 2-warp blocks, as many as are resident per SM at once (shared memory
+  // and registers; the occupancy calculator's answer, asked once).
+  static int bps_cache[2] = {0, 0};
+  int& bps = bps_cache[d.kv8 != nullptr ? 1 : 0];
+  if (bps == 0) {
+    const cudaError_t e = d.kv8 != nullptr
+        ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, battn_kernel<true>, kBAttnWarps * 32, attn_smem_bytes<true>())
+        : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, battn_kernel<false>, kBAttnWarps * 32, attn_smem_bytes<false>());
+    if (e != cudaSuccess || bps < 1) { bps = 0; return ::MK_ERR_LAUNCH; }
+  }
+  const int attn_blocks = s->sms * bps;
+  // Chunks per attention item: split each (sequence, head) into as many
+  // spans as there are warp slots for all of them at once, at the
+  // engine's capacity; never more items than slots (a second wave of items
+  // would double the layer's attention time).
+  const int per_pair = std::max(1, s->sms * bps * kBAttnWarps / (d.batch * kBNKV));
+  const int attn_span = (d.maxch + per_pair - 1) / per_pair;
   const bool f8 = d.kv8 != nullptr;
   // Split-K factors of the q/k/v, O, gate/up and down GEMMs (cluster
   // split K, partials pushed into rank 0's shared memory).  Measured on B200
