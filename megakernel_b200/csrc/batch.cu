@@ -1137,10 +1137,11 @@ int batch_step(BatchState* s, const int* forced, const int* prev_out, int* out, 
   // (64 sequences at position 1024, ms per step): {1, 2, 1, 3} 2.049,
   // {1, 2, 1, 4} 2.030, {1, 1, 1, 4} 2.095, {2, 2, 1, 4} 2.033,
   // {1, 2, 2, 4} 2.178, {2, 2, 2, 4} 2.164; with the 256-column LM head,
-  // {1, 2, 1, 4} 1.963 and {2, 2, 1, 4} 1.957 (kept).  (The earlier form -- partials
+  // {1, 2, 1, 4} 1.963 and {2, 2, 1, 4} 1.957, but over the bench's 256
+  // steps (positions 1024-1279) 2.007 and 2.015: {1, 2, 1, 4} kept.  (The earlier form -- partials
   // through global memory, a ticket, the last CTA summing, epilogue inputs
   // loaded after the MMAs -- took 2.463 at {1, 2, 1, 3}.)
-  int ks[4] = {2, 2, 1, 4};
+  int ks[4] = {1, 2, 1, 4};
   if (const char* e = getenv("MK_BATCH_KSPLIT")) {
     int t[4];
     if (sscanf(e, "%d,%d,%d,%d", &t[0], &t[1], &t[2], &t[3]) == 4)
