@@ -162,7 +162,7 @@ __global__ void bembed_kernel(BatchDev d, const __nv_bfloat16* __restrict__ emb,
 // value head t-24.  Scales by 1/rms, applies q_norm / k_norm and RoPE at the
 // sequence's position, writes q (fp32) or appends K / V (bf16) to the cache.
 struct EpiQKV {
-  static constexpr bool kCols = false;
+  static constexpr bool kCols = true;
   // Prefetched inputs depend on the tile index (re-fetched per 64-column tile).
   static constexpr bool kPrePerTile = true;
   // pre: [0, 64) 1/rms per row, [64, 128) head-norm gains, [128, 192) the
@@ -192,60 +192,80 @@ struct EpiQKV {
       for (int c = 0; c < 32; c += 4) *reinterpret_cast<float4*>(dst + c) = __ldg(reinterpret_cast<const float4*>(src + c));
     }
   }
-  __device__ __forceinline__ static void apply(const Params& ep, int t, int seq, float (&v)[64], const float* pre) {
+  __device__ __forceinline__ static void apply(const Params&, int, int, float (&)[64], const float*) {}
+  // 128 threads, two per row (lanes 2r, 2r + 1 of a warp pair up): thread
+  // half h takes columns [16h, 16h + 16) and their RoPE partners 32 on, so
+  // the head norm's sum of squares is one shuffle and every RoPE pair stays
+  // in one thread.
+  __device__ __forceinline__ static void cols(const Params& ep, int t, float* tile, int tid, const float* pre,
+                                              int ra, int rb) {
     const BatchDev& d = ep.d;
-    if (seq >= d.batch) return;
-    const float r = pre[seq];
+    const int row = ra + (tid >> 1), h = tid & 1, c0 = 16 * h;
+    const bool live = row < rb && row < d.batch;
+    const int rr_ = live ? row : ra;            // a valid row for the (unused) loads of idle threads
+    const float r = pre[rr_];
+    float a[16], b[16];
+    const float4* tr = reinterpret_cast<const float4*>(tile + rr_ * kTcCombStride);
 #pragma unroll
-    for (int c = 0; c < 64; ++c) v[c] *= r;
-    const int p = __float_as_int(pre[128 + seq]);
+    for (int k = 0; k < 4; ++k) {
+      const float4 x = tr[(c0 >> 2) + k], y = tr[8 + (c0 >> 2) + k];
+      a[4 * k] = x.x * r; a[4 * k + 1] = x.y * r; a[4 * k + 2] = x.z * r; a[4 * k + 3] = x.w * r;
+      b[4 * k] = y.x * r; b[4 * k + 1] = y.y * r; b[4 * k + 2] = y.z * r; b[4 * k + 3] = y.w * r;
+    }
     if (t < 24) {
-      const float* gn = pre + 64;
       float ss = 0.f;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) ss = fmaf(v[c], v[c], ss);
+      for (int c = 0; c < 16; ++c) ss = fmaf(b[c], b[c], fmaf(a[c], a[c], ss));
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       const float rr = rsqrtf(ss / 64.f + 1e-6f);
+      const float* gn = pre + 64;
+      const float* cs = pre + 192 + 64 * rr_;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) v[c] = gn[c] * (v[c] * rr);
-      const float* cs = pre + 192 + 64 * seq;
-      const float* sn = cs + 32;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float x0 = v[c], x1 = v[c + 32], cc = cs[c], ssn = sn[c];
-        v[c] = x0 * cc - x1 * ssn;
-        v[c + 32] = x1 * cc + x0 * ssn;
+      for (int c = 0; c < 16; ++c) {
+        const float x0 = gn[c0 + c] * (a[c] * rr), x1 = gn[32 + c0 + c] * (b[c] * rr);
+        const float cc = cs[c0 + c], sn = cs[32 + c0 + c];
+        a[c] = x0 * cc - x1 * sn;
+        b[c] = x1 * cc + x0 * sn;
       }
     }
+    if (!live) return;
+    const int p = __float_as_int(pre[128 + row]);
     if (t < 16) {
-      float* o = d.q + ((size_t)seq * kBNQ + t) * kBD;
+      float* o = d.q + ((size_t)row * kBNQ + t) * kBD;
 #pragma unroll
-      for (int c = 0; c < 64; c += 4) *reinterpret_cast<float4*>(o + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
-    } else {
-      const int kv = t < 24 ? 0 : 1, h = t < 24 ? t - 16 : t - 24;
-      if (d.kv8 != nullptr) {
-        // fp8 cache: e4m3, round to nearest, saturating (|K|, |V| << 448).
-        uint8_t* o8 = d.kv8 + bkv_index(d, seq, ep.l, kv, h, p);
-#pragma unroll
-        for (int c = 0; c < 64; c += 16) {
-          uint4 w;
-          w.x = (uint32_t)f32x2_to_e4m3x2(v[c], v[c + 1]) | ((uint32_t)f32x2_to_e4m3x2(v[c + 2], v[c + 3]) << 16);
-          w.y = (uint32_t)f32x2_to_e4m3x2(v[c + 4], v[c + 5]) | ((uint32_t)f32x2_to_e4m3x2(v[c + 6], v[c + 7]) << 16);
-          w.z = (uint32_t)f32x2_to_e4m3x2(v[c + 8], v[c + 9]) | ((uint32_t)f32x2_to_e4m3x2(v[c + 10], v[c + 11]) << 16);
-          w.w = (uint32_t)f32x2_to_e4m3x2(v[c + 12], v[c + 13]) | ((uint32_t)f32x2_to_e4m3x2(v[c + 14], v[c + 15]) << 16);
-          *reinterpret_cast<uint4*>(o8 + c) = w;
-        }
-        return;
+      for (int c = 0; c < 16; c += 4) {
+        *reinterpret_cast<float4*>(o + c0 + c) = make_float4(a[c], a[c + 1], a[c + 2], a[c + 3]);
+        *reinterpret_cast<float4*>(o + 32 + c0 + c) = make_float4(b[c], b[c + 1], b[c + 2], b[c + 3]);
       }
-      __nv_bfloat16* o = d.kv + bkv_index(d, seq, ep.l, kv, h, p);
+      return;
+    }
+    const int kv = t < 24 ? 0 : 1, hd = t < 24 ? t - 16 : t - 24;
+    if (d.kv8 != nullptr) {
+      // fp8 cache: e4m3, round to nearest, saturating (|K|, |V| << 448).
+      uint8_t* o8 = d.kv8 + bkv_index(d, row, ep.l, kv, hd, p);
+      uint4 w;
+      w.x = (uint32_t)f32x2_to_e4m3x2(a[0], a[1]) | ((uint32_t)f32x2_to_e4m3x2(a[2], a[3]) << 16);
+      w.y = (uint32_t)f32x2_to_e4m3x2(a[4], a[5]) | ((uint32_t)f32x2_to_e4m3x2(a[6], a[7]) << 16);
+      w.z = (uint32_t)f32x2_to_e4m3x2(a[8], a[9]) | ((uint32_t)f32x2_to_e4m3x2(a[10], a[11]) << 16);
+      w.w = (uint32_t)f32x2_to_e4m3x2(a[12], a[13]) | ((uint32_t)f32x2_to_e4m3x2(a[14], a[15]) << 16);
+      *reinterpret_cast<uint4*>(o8 + c0) = w;
+      w.x = (uint32_t)f32x2_to_e4m3x2(b[0], b[1]) | ((uint32_t)f32x2_to_e4m3x2(b[2], b[3]) << 16);
+      w.y = (uint32_t)f32x2_to_e4m3x2(b[4], b[5]) | ((uint32_t)f32x2_to_e4m3x2(b[6], b[7]) << 16);
+      w.z = (uint32_t)f32x2_to_e4m3x2(b[8], b[9]) | ((uint32_t)f32x2_to_e4m3x2(b[10], b[11]) << 16);
+      w.w = (uint32_t)f32x2_to_e4m3x2(b[12], b[13]) | ((uint32_t)f32x2_to_e4m3x2(b[14], b[15]) << 16);
+      *reinterpret_cast<uint4*>(o8 + 32 + c0) = w;
+      return;
+    }
+    __nv_bfloat16* o = d.kv + bkv_index(d, row, ep.l, kv, hd, p);
 #pragma unroll
-      for (int c = 0; c < 64; c += 8) {
-        uint4 w;
-        w.x = pack_bf16x2(v[c], v[c + 1]);
-        w.y = pack_bf16x2(v[c + 2], v[c + 3]);
-        w.z = pack_bf16x2(v[c + 4], v[c + 5]);
-        w.w = pack_bf16x2(v[c + 6], v[c + 7]);
-        *reinterpret_cast<uint4*>(o + c) = w;
-      }
+    for (int c = 0; c < 16; c += 8) {
+      uint4 w;
+      w.x = pack_bf16x2(a[c], a[c + 1]); w.y = pack_bf16x2(a[c + 2], a[c + 3]);
+      w.z = pack_bf16x2(a[c + 4], a[c + 5]); w.w = pack_bf16x2(a[c + 6], a[c + 7]);
+      *reinterpret_cast<uint4*>(o + c0 + c) = w;
+      w.x = pack_bf16x2(b[c], b[c + 1]); w.y = pack_bf16x2(b[c + 2], b[c + 3]);
+      w.z = pack_bf16x2(b[c + 4], b[c + 5]); w.w = pack_bf16x2(b[c + 6], b[c + 7]);
+      *reinterpret_cast<uint4*>(o + 32 + c0 + c) = w;
     }
   }
 };
